@@ -1,0 +1,469 @@
+#!/usr/bin/env python3
+"""Benchmark driver: GEMM TFLOPS and % of the measured UMMA dense peak on B200.
+
+Default workload (the metric's configuration): bf16 GEMM
+M = N = K = 8192, A row-major, B N x K, D column-major bf16, seeded
+uniform[-1,1) inputs, fp32 accumulation, 1-SM tcgen05 tile 128x256x64 with
+the deepest stage count that fits (4).  One step = one GEMM (one launch of the
+library kernel through the C ABI).  At N GPUs the GEMM is N-split with a
+fixed 8192-column slab per GPU (A replicated, B and D column-sliced, no
+collective on the data path): weak scaling, value = total FLOPs / max-over-
+ranks time.
+
+``--impl reference`` times the CPU path the reference lacks and the benchmark
+plan names as its stand-in: the OpenMP fp32-accumulate host GEMM of oracle/
+(cpu_gemm.c), on a bounded slab of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG_DIR = ROOT / "microbench-blackwell_b200"
+
+# Reference figures used in derived keys (cited, not measured here).
+REF_UMMA_FLOP_PER_CLK_SM = {  # umma_throughput/tput_results_max.csv:13,49 (1SM M128 N256 SS)
+    "bf16": 8152.85, "e4m3": 16344.5, "nvfp4": 32721.7}
+REF_SINGLE_CTA_TFLOPS = {"bf16": 10.4596, "e4m3": 20.6377}  # cutlass_gemm_mainloop/results.csv:461,938
+
+WORKLOADS = {
+    # name: dtype, M, N (per GPU), K, knobs, inputs
+    "bf16_8192": dict(dtype="bf16", m=8192, n=8192, k=8192,
+                      knobs=dict(tile_n=256, tile_k=64, stages=4, cta_group=1),
+                      a=("uniform", 1.0), b=("uniform", 1.0), config=2),
+    "e4m3_16384_2sm": dict(dtype="e4m3", m=16384, n=16384, k=16384,
+                           knobs=dict(tile_n=256, tile_k=128, stages=0, cta_group=2),
+                           a=("normal", 0.25), b=("normal", 0.25), config=3),
+    "nvfp4_mlp": dict(dtype="nvfp4", m=8192, n=28672, k=8192,
+                      knobs=dict(tile_n=192, tile_k=256, stages=0, cta_group=1),
+                      a=("normal", 1.0), b=("normal", 1.0), config=4),
+    "e4m3_nsplit": dict(dtype="e4m3", m=16384, n=57344, k=8192,
+                        knobs=dict(tile_n=256, tile_k=128, stages=0, cta_group=2),
+                        a=("normal", 0.25), b=("normal", 0.02), config=5),
+    "bf16_256": dict(dtype="bf16", m=256, n=256, k=256,
+                     knobs=dict(tile_n=256, tile_k=64, stages=4, cta_group=1),
+                     a=("uniform", 1.0), b=("uniform", 1.0), config=1),
+}
+
+
+def load_pkg():
+    name = "microbench_blackwell_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, PKG_DIR / "__init__.py",
+                                                  submodule_search_locations=[str(PKG_DIR)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["source"] = "measured"
+        return d
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "sm_max_mhz": 1965.0, "source": "fallback"}
+
+
+def ncu_traffic(workload: str):
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.exists():
+        return json.loads(p.read_text()).get(workload)
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Polls NVML (read-only) every few ms on this rank's GPU during the timed region."""
+
+    REASONS = {"sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+               "hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "hw_power_brake_slowdown": "nvmlClocksEventReasonHwPowerBrakeSlowdown"}
+
+    def __init__(self, torch_device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml as N
+            import torch
+            N.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(torch_device_index).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            self.h = N.nvmlDeviceGetHandleByUUID(uuid.encode() if isinstance(uuid, str) else uuid)
+            self.N = N
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML missing: report no clocks rather than guess
+            self.err = repr(e)
+            self.max_mhz = None
+
+    def _run(self):
+        N = self.N
+        masks = {k: getattr(N, v) for k, v in self.REASONS.items() if hasattr(N, v)}
+        while not self._stop.is_set():
+            try:
+                self.samples.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+                r = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, m in masks.items():
+                    if r & m:
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self) -> dict:
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ helpers
+def dist_code(pkg, name: str) -> int:
+    return pkg.UNIFORM if name == "uniform" else pkg.NORMAL
+
+
+def dtype_code(pkg, name: str) -> int:
+    return {"bf16": pkg.BF16, "e4m3": pkg.FP8_E4M3, "nvfp4": pkg.NVFP4}[name]
+
+
+def elem_bytes(name: str) -> float:
+    return {"bf16": 2.0, "e4m3": 1.0, "nvfp4": 0.5}[name]
+
+
+def cpu_gemm_sample(wl: dict, budget_s: float, seed: int = 0):
+    """Time the oracle's OpenMP GEMM on a slab of rows of A against all of B (dequantised fp32)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import oracle as O
+    m, n, k, dt = wl["m"], wl["n"], wl["k"], wl["dtype"]
+    # B is the large operand; limit it to at most 8192 rows so setup stays bounded.
+    nb = min(n, 8192)
+    if dt == "nvfp4":
+        pb, sb = O.generate_nvfp4(nb, k, wl["b"][1], seed, 1)
+        B = O.dequant_nvfp4(pb, sb, k)
+    else:
+        odt = O.BF16 if dt == "bf16" else O.FP8_E4M3
+        B = O.dequant(O.generate(nb, k, odt, 0 if wl["b"][0] == "uniform" else 1, wl["b"][1], seed, 1), odt)
+    rows = 16
+    while True:
+        if dt == "nvfp4":
+            pa, sa = O.generate_nvfp4(max(rows, 128), k, wl["a"][1], seed, 0)
+            A = O.dequant_nvfp4(pa, sa, k)[:rows]
+        else:
+            A = O.dequant(O.generate(rows, k, odt, 0 if wl["a"][0] == "uniform" else 1, wl["a"][1], seed, 0), odt)
+        t0 = time.perf_counter()
+        O.gemm_omp_f32(A, B)
+        dt_s = time.perf_counter() - t0
+        if dt_s * 4 > budget_s or rows >= m:
+            break
+        rows = min(m, rows * 4)
+    flops = 2.0 * rows * nb * k
+    return {"value": flops / dt_s / 1e12, "unit": "TFLOPS", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{rows} x {nb} x {k} slab of the {m}x{n}x{k} {dt} GEMM "
+                      f"(oracle/cpu_gemm.c OpenMP fp32-accumulate over dequantised inputs), {dt_s:.2f} s"}, dt_s
+
+
+def host_note_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args, wl, rank: int, world: int):
+    if rank != 0:
+        return
+    budget = 8.0
+    per_step = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        cb, secs = cpu_gemm_sample(wl, budget_s=budget / 4)
+        if i >= args.warmup:
+            per_step.append(cb["value"])
+        info = cb
+    value = statistics.median(per_step)
+    info["value"] = value
+    line = {"metric": "GEMM TFLOPS", "impl": "reference", "value": value, "unit": "TFLOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": wl["dtype"], "data": "synthetic (seeded)",
+            "config": config_block(wl, world, args),
+            "cpu_baseline": info,
+            "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference has no CPU GEMM; this arm times oracle/cpu_gemm.c (OpenMP host GEMM) "
+                    "on a row slab, host cores only"}
+    print(json.dumps(line), flush=True)
+
+
+def config_block(wl, world, args):
+    return {"workload": args.workload, "baseline_config": wl["config"],
+            "m": wl["m"], "n_per_gpu": wl["n"], "n_total": wl["n"] * world, "k": wl["k"],
+            "dtype": wl["dtype"], **{k: v for k, v in wl["knobs"].items()},
+            "parallelism": f"nsplit{world}" if world > 1 else "single",
+            "layout": "A row-major MxK, B NxK (K-major), D column-major bf16",
+            "l2": "inputs larger than L2 (126 MB), no flush" if wl["m"] * wl["k"] * elem_bytes(wl["dtype"]) +
+                  wl["n"] * wl["k"] * elem_bytes(wl["dtype"]) > 126e6 else "inputs fit in L2 (latency-bound KAT)"}
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, wl, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+    pkg = load_pkg()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    st = stream.cuda_stream
+    dt = dtype_code(pkg, wl["dtype"])
+    m, n, k = wl["m"], wl["n"], wl["k"]
+    knobs = dict(wl["knobs"])
+    if args.stages is not None:
+        knobs["stages"] = args.stages
+    if args.tile_n is not None:
+        knobs["tile_n"] = args.tile_n
+    n0 = rank * n
+    with torch.cuda.stream(stream):
+        ops = pkg.make_operands(dt, m, n, k, seed=args.seed,
+                                a_dist=dist_code(pkg, wl["a"][0]), a_scale=wl["a"][1],
+                                b_dist=dist_code(pkg, wl["b"][0]), b_scale=wl["b"][1],
+                                n0=n0, device=dev, stream=st)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    gargs = pkg.make_args(dtype=dt, m=m, n=n, k=k, a=ops.a.data_ptr(), b=ops.b.data_ptr(),
+                          d=ops.d.data_ptr(), sfa=None if ops.sfa is None else ops.sfa.data_ptr(),
+                          sfb=None if ops.sfb is None else ops.sfb.data_ptr(),
+                          status=status.data_ptr(), **knobs)
+    rc, info = pkg.query(gargs)
+    if rc != pkg.OK:
+        raise SystemExit(f"cannot implement: {info.reason.decode()}")
+    L = pkg.lib()
+    launch = L.gemm_sm100a_launch
+    argp = C.byref(gargs)
+    sp = C.c_void_p(st)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    # warm-up
+    for _ in range(args.warmup):
+        if launch(argp, sp) != 0:
+            raise SystemExit("launch failed")
+    stream.synchronize()
+    rc, detail = pkg.read_status(status.data_ptr(), st)
+    if rc != 0:
+        raise SystemExit(f"device status error 0x{detail & 0xffffffff:08x}")
+
+    # timed region: K launches bracketed by barrier + synchronize, events on the launching stream
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with sampler:
+        start.record(stream)
+        for _ in range(args.steps):
+            launch(argp, sp)
+        end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    rc, detail = pkg.read_status(status.data_ptr(), st)
+    if rc != 0:
+        raise SystemExit(f"device status error 0x{detail & 0xffffffff:08x}")
+    flop = pkg.flops(m, n, k)
+    ms_per_step = ms_max / args.steps
+    value = flop * world / (ms_per_step * 1e-3) / 1e12
+    achieved = flop / (ms / args.steps * 1e-3) / 1e12          # this rank's kernel, per launch
+    clocks = sampler.summary()
+
+    # ---------------------------------------------------------- end to end (host buffers)
+    e2e = run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank)
+
+    # ---------------------------------------------------------- single-CTA mainloop (reference experiment)
+    single = run_single_cta(pkg, wl, dev, stream) if (rank == 0 and wl["dtype"] in REF_SINGLE_CTA_TFLOPS) else None
+
+    if rank != 0:
+        return
+    peaks = measured_peaks()
+    sm_mhz = clocks.get("sm_mhz")
+    umma = REF_UMMA_FLOP_PER_CLK_SM[wl["dtype"]]
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu, _ = cpu_gemm_sample(wl, budget_s=12.0, seed=args.seed)
+    peak_key = "bf16_tflops" if wl["dtype"] == "bf16" else None
+    line = {
+        "metric": "GEMM TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": wl["dtype"], "data": "synthetic (seeded, generated on device)",
+        "config": config_block(wl, world, args),
+        "roofline": {"bound": "tensor", "achieved": achieved,
+                     "peak": peaks["bf16_tflops"] if peak_key else None,
+                     "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"] if peak_key else None,
+                     "peak_source": f"{peaks['source']} cuBLAS bf16 burst (MEASURED_PEAKS.json)",
+                     "traffic": ncu_traffic(args.workload),
+                     "algorithmic_bytes": m * k * elem_bytes(wl["dtype"]) + n * k * elem_bytes(wl["dtype"]) + m * n * 2},
+        "sol_umma": {"pct": (100.0 * achieved / (umma * 148 * sm_mhz * 1e6 / 1e12)) if sm_mhz else None,
+                     "flop_per_clk_per_sm": umma, "sm_mhz": sm_mhz,
+                     "source": "reference umma_throughput/tput_results_max.csv (1SM M128 N256 SS)"},
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "cpu_baseline": cpu,
+        "single_cta": single,
+        "kernel": {"grid": info.grid_ctas, "stages": info.stages, "tile": [info.tile_m, info.tile_n, info.tile_k],
+                   "smem_bytes": info.smem_bytes, "tmem_columns": info.tmem_columns},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank):
+    """Same GEMM through the C ABI with the inputs in pinned host memory and the
+    result read back every step (copies inside the timed region)."""
+    import torch
+    import torch.distributed as dist
+    steps = max(3, min(args.steps, 10))
+    ha = torch.empty_like(ops.a, device="cpu").pin_memory()
+    hb = torch.empty_like(ops.b, device="cpu").pin_memory()
+    hd = torch.empty_like(ops.d, device="cpu").pin_memory()
+    ha.copy_(ops.a); hb.copy_(ops.b)
+    extra = []
+    if ops.sfa is not None:
+        hsa = torch.empty_like(ops.sfa, device="cpu").pin_memory(); hsa.copy_(ops.sfa)
+        hsb = torch.empty_like(ops.sfb, device="cpu").pin_memory(); hsb.copy_(ops.sfb)
+        extra = [(hsa, ops.sfa), (hsb, ops.sfb)]
+    h2d = ha.numel() * ha.element_size() + hb.numel() * hb.element_size() + \
+        sum(h.numel() for h, _ in extra)
+    d2h = hd.numel() * hd.element_size()
+    L = pkg.lib()
+    argp = C.byref(gargs)
+    sp = C.c_void_p(stream.cuda_stream)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            ops.a.copy_(ha, non_blocking=True)
+            ops.b.copy_(hb, non_blocking=True)
+            for h, d in extra:
+                d.copy_(h, non_blocking=True)
+            L.gemm_sm100a_launch(argp, sp)
+            hd.copy_(ops.d, non_blocking=True)
+        end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / steps
+    flop = pkg.flops(ops.m, ops.n, ops.k) * world
+    return {"value": flop / (ms_step * 1e-3) / 1e12, "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps, "ms_per_step": ms_step,
+            "path": "pinned host A,B -> gemm_sm100a_launch -> pinned host D, one stream"}
+
+
+def run_single_cta(pkg, wl, dev, stream):
+    """The reference experiment: one CTA, M=TILE_M, N=TILE_N, K=131072, 1 warm-up + 20 timed
+    (cutlass_gemm_bench.cu:158-257).  Inputs are seeded (the reference zero-fills)."""
+    import torch
+    dt = dtype_code(pkg, wl["dtype"])
+    tn = 256
+    tk = 64 if wl["dtype"] == "bf16" else 128
+    K = 131072
+    ops = pkg.make_operands(dt, 128, tn, K, seed=1, device=dev, stream=stream.cuda_stream)
+    g = pkg.make_args(dtype=dt, m=128, n=tn, k=K, a=ops.a.data_ptr(), b=ops.b.data_ptr(), d=ops.d.data_ptr(),
+                      tile_n=tn, tile_k=tk, stages=4, max_ctas=1)
+    L = pkg.lib()
+    sp = C.c_void_p(stream.cuda_stream)
+    L.gemm_sm100a_launch(C.byref(g), sp)
+    stream.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(20):
+        L.gemm_sm100a_launch(C.byref(g), sp)
+    e.record(stream)
+    e.synchronize()
+    ms = s.elapsed_time(e) / 20
+    tf = 2.0 * 128 * tn * K / (ms * 1e-3) / 1e12
+    return {"tile": [128, tn, tk], "stages": 4, "k": K, "time_ms": ms, "tflops": tf,
+            "reference_published_tflops": REF_SINGLE_CTA_TFLOPS[wl["dtype"]],
+            "ratio_vs_reference": tf / REF_SINGLE_CTA_TFLOPS[wl["dtype"]]}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bf16_8192")
+    ap.add_argument("--stages", type=int, default=None)
+    ap.add_argument("--tile-n", type=int, default=None)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    wl = WORKLOADS[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}; using WORLD_SIZE", file=sys.stderr)
+
+    if args.impl == "reference":
+        run_reference(args, wl, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, wl, rank, world, local_rank)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

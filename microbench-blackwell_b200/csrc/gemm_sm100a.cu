@@ -1,0 +1,707 @@
+// gemm_sm100a.cu -- persistent warp-specialised dense GEMM for B200 (sm_100a).
+//
+// Replaces the CUTLASS SM100 GEMM instantiated by the reference benchmark
+// (cutlass_gemm_mainloop/cutlass_gemm_bench.cu:101-156: CollectiveBuilder with
+// KernelTmaWarpSpecialized1SmSm100 mainloop + NoSmemWarpSpecialized1Sm
+// epilogue) with a hand-written kernel of the same math
+//     D(bf16, column-major) = alpha * A(row-major) . B(N x K)^T, fp32 accumulate
+// for bf16, fp8 e4m3 and NVFP4 (e2m1 + ue4m3 per-16 scales) operands, in
+// 1-SM (cta_group::1, 128 x BN) and 2-SM (cta_group::2, 256 x BN per CTA pair)
+// forms.
+//
+// One CTA of 192 threads per SM (persistent over output tiles):
+//   warp 0      TMA producer: 128B-swizzled A/B k-atoms into a STAGES-deep
+//               shared-memory ring, guarded by full/empty mbarriers.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer; commits
+//               free ring slots and hands finished accumulators to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (32 lanes each),
+//               alpha scale, bf16 round, coalesced column-major stores.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the mainloop of tile i+1.
+//
+// Every mbarrier wait is bounded (globaltimer budget): on expiry the kernel
+// records a status word, tells the other roles to stop, drains its own
+// in-flight copies / MMAs with a bounded wait, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "gemm_sm100a.h"
+#include "sm100_ptx.cuh"
+
+using namespace sm100;
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kSmemLimit = 232448;      // 227 KiB of opt-in dynamic shared memory per CTA
+constexpr int kBarrierBytes = 1024;     // barrier block + bookkeeping words
+constexpr int kMaxStages = 32;
+
+enum Role : uint32_t { ROLE_PRODUCER = 1, ROLE_MMA = 2, ROLE_EPILOGUE = 3, ROLE_DRAIN = 4 };
+
+struct KernelParams {
+  int32_t m, n, k;
+  int32_t num_m_units, num_n_units, num_units;
+  int32_t num_k_blocks;
+  int32_t atoms;          // 128-byte K atoms per stage
+  int32_t stages;
+  int32_t raster_group;
+  int32_t tmem_cols;
+  uint32_t stage_bytes;   // per CTA: A + B (+ scale factors)
+  uint32_t a_atom_bytes, b_atom_bytes;
+  uint32_t sf_stage_bytes;  // NVFP4: SFA + SFB bytes per stage per CTA
+  uint32_t idesc;
+  float alpha;
+  __nv_bfloat16* d;
+  int64_t ldd;
+  int32_t* status;
+  uint64_t timeout_ns;
+  uint32_t flags;
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int32_t sf_kblocks;     // K / 64 (NVFP4 scale atoms along K)
+};
+
+// Elements of each dtype in one 128-byte swizzle atom row.
+__host__ __device__ constexpr int atom_elems(int dt) { return dt == 0 ? 64 : (dt == 1 ? 128 : 256); }
+
+// tcgen05 instruction descriptor.
+//  dense (kind::f16 / kind::f8f6f4): [4,6) D format (1 = F32), [7,10) A format,
+//    [10,13) B format (BF16 = 1 for kind::f16, E4M3 = 0 for kind::f8f6f4),
+//    [15] / [16] A / B major (0 = K), [17,23) N >> 3, [24,29) M >> 4.
+//  block-scaled (kind::mxf4nvf4): [4,6) B scale id, [7,10) A format (E2M1 = 1),
+//    [10,12) B format, [17,23) N >> 3, [23] scale type (0 = UE4M3),
+//    [24,29) M >> 4, [29,31) A scale id, [31] K = 64.
+__host__ __device__ constexpr uint32_t make_idesc(int dt, int mma_m, int mma_n) {
+  uint32_t d = 0;
+  if (dt == 2) {
+    d |= 1u << 7;
+    d |= 1u << 10;
+    d |= (uint32_t)(mma_n >> 3) << 17;
+    d |= (uint32_t)(mma_m >> 4) << 24;
+  } else {
+    const uint32_t fmt = dt == 0 ? 1u : 0u;
+    d |= 1u << 4;
+    d |= fmt << 7;
+    d |= fmt << 10;
+    d |= (uint32_t)(mma_n >> 3) << 17;
+    d |= (uint32_t)(mma_m >> 4) << 24;
+  }
+  return d;
+}
+
+struct SharedCtl {
+  uint32_t abort_addr;     // local abort flag (shared::cta address)
+  uint32_t abort_peer;     // the pair peer's abort flag (shared::cluster), 0 if none
+  uint64_t timeout_ns;
+  int32_t* status;
+};
+
+__device__ __noinline__ void raise_abort(const SharedCtl& c, uint32_t role, uint32_t idx) {
+  if (c.status) {
+    const int32_t code = (int32_t)(0x3u | (role << 8) | ((idx & 0xFFu) << 12) | ((blockIdx.x & 0x7FFu) << 20));
+    atomicCAS(c.status, 0, code);
+  }
+  st_shared_u32(c.abort_addr, 1u);
+  if (c.abort_peer) st_shared_cluster_u32(c.abort_peer, 1u);
+}
+
+// Bounded wait for phase `parity` of mbarrier `bar`; false when aborted.
+template <bool kCluster>
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const SharedCtl& c,
+                                         uint32_t role, uint32_t idx) {
+  if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    if (ld_shared_volatile_u32(c.abort_addr)) return false;
+    if (globaltimer_ns() - t0 > c.timeout_ns) {
+      raise_abort(c, role, idx);
+      return false;
+    }
+  }
+}
+
+// Wait with a short fixed budget during abort drains; never raises.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64_t budget_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > budget_ns) break;
+  }
+}
+
+__device__ __forceinline__ void unit_coords(int u, const KernelParams& p, int& um, int& un) {
+  const int G = p.raster_group;
+  const int per_group = G * p.num_n_units;
+  const int g = u / per_group;
+  const int first_m = g * G;
+  const int rows = min(p.num_m_units - first_m, G);
+  const int r = u - g * per_group;
+  um = first_m + r % rows;
+  un = r / rows;
+}
+
+// ----------------------------------------------------------------------------
+// The kernel.  DT: 0 bf16, 1 e4m3, 2 NVFP4.  CG: 1 or 2 (CTA pair).  BN: MMA N
+// (the pair's full N for CG = 2; each CTA of the pair loads BN / 2 rows of B).
+// ----------------------------------------------------------------------------
+template <int DT, int CG, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b,
+                   const __grid_constant__ KernelParams p) {
+  constexpr int BM = 128;                 // A rows per CTA (= TMEM lanes)
+  constexpr int BN_CTA = BN / CG;         // B rows per CTA
+  constexpr int MMA_M = BM * CG;
+  constexpr int KIND = DT == 0 ? 0 : 1;
+  constexpr int MAP_ELEMS_PER_ATOM = DT == 0 ? 64 : 128;  // tensor-map elements per 128 B
+  constexpr int SF_COLS_A = 4;            // TMEM columns of SFA per 64-element K step (NVFP4)
+  constexpr int SF_COLS_B = ((BN + 127) / 128) * 4;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* const base_ptr = smem_raw + (base - raw_base);
+
+  const uint32_t ring = base;
+  const uint32_t bars = base + (uint32_t)p.stages * p.stage_bytes;
+  const uint32_t full_bar = bars;                         // [stages]
+  const uint32_t empty_bar = bars + 8u * kMaxStages;      // [stages]
+  const uint32_t tfull_bar = bars + 16u * kMaxStages;     // [2]
+  const uint32_t tempty_bar = tfull_bar + 16u;            // [2]
+  const uint32_t drain_bar = tempty_bar + 16u;
+  const uint32_t tmem_slot = drain_bar + 8u;
+  const uint32_t abort_flag = tmem_slot + 4u;
+  uint32_t* const tmem_slot_ptr = reinterpret_cast<uint32_t*>(base_ptr + (tmem_slot - base));
+
+  const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t cta_rank = CG == 2 ? cluster_ctarank() : 0u;
+  const bool leader = cta_rank == 0;
+  const int pair = (int)(blockIdx.x / CG);
+  const int num_pairs = (int)(gridDim.x / CG);
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(full_bar + 8u * s, 1);
+      mbar_init(empty_bar + 8u * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar + 8u * a, 1);
+      mbar_init(tempty_bar + 8u * a, 4 * CG);   // one arrive per epilogue warp of the pair
+    }
+    mbar_init(drain_bar, 1);
+    st_shared_u32(abort_flag, 0u);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(tmem_slot, (uint32_t)p.tmem_cols);
+    tmem_relinquish<CG>();
+  }
+  tc_fence_before();
+  if constexpr (CG == 2) { cluster_arrive(); cluster_wait(); } else { __syncthreads(); }
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot_ptr);
+
+  SharedCtl ctl;
+  ctl.abort_addr = abort_flag;
+  ctl.abort_peer = CG == 2 ? mapa_shared(abort_flag, cta_rank ^ 1u) : 0u;
+  ctl.timeout_ns = p.timeout_ns;
+  ctl.status = p.status;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && !(p.flags & GEMM_FLAG_INJECT_STALL)) {
+      const uint64_t policy = policy_evict_normal();
+      const uint32_t leader_full = CG == 2 ? mapa_shared(full_bar, 0) : full_bar;
+      const uint32_t tx_bytes = p.stage_bytes * CG;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int u = pair; u < p.num_units && ok; u += num_pairs) {
+        int um, un;
+        unit_coords(u, p, um, un);
+        const int32_t m0 = um * MMA_M + (int32_t)cta_rank * BM;
+        const int32_t n0 = un * BN + (int32_t)cta_rank * BN_CTA;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!wait_bar<false>(empty_bar + 8u * stage, phase ^ 1u, ctl, ROLE_PRODUCER, stage)) { ok = false; break; }
+          const uint32_t sbase = ring + (uint32_t)stage * p.stage_bytes;
+          const uint32_t fb = full_bar + 8u * stage;
+          if (leader) mbar_arrive_expect_tx(fb, tx_bytes);
+          const uint32_t target = CG == 2 ? leader_full + 8u * stage : fb;
+          for (int ka = 0; ka < p.atoms; ++ka) {
+            const int32_t x = (kb * p.atoms + ka) * MAP_ELEMS_PER_ATOM;
+            const uint32_t a_dst = sbase + (uint32_t)ka * p.a_atom_bytes;
+            const uint32_t b_dst = sbase + (uint32_t)p.atoms * p.a_atom_bytes + (uint32_t)ka * p.b_atom_bytes;
+            if constexpr (CG == 2) {
+              tma_load_2d_pair(a_dst, &tmap_a, target, x, m0, policy);
+              tma_load_2d_pair(b_dst, &tmap_b, target, x, n0, policy);
+            } else {
+              tma_load_2d(a_dst, &tmap_a, target, x, m0, policy);
+              tma_load_2d(b_dst, &tmap_b, target, x, n0, policy);
+            }
+          }
+          if constexpr (DT == 2) {
+            // Scale factors: one 512-byte atom (128 rows x 4 scales) per 64 K
+            // elements; a stage covers atoms*4 of them for A, and for B
+            // ceil(BN_CTA/128) row blocks each.
+            const uint32_t sf_base = sbase + (uint32_t)p.atoms * (p.a_atom_bytes + p.b_atom_bytes);
+            const int kq0 = kb * p.atoms * 4;
+            const int nsf = p.atoms * 4;
+            const uint8_t* sfa_src = p.sfa + ((int64_t)(m0 / 128) * p.sf_kblocks + kq0) * 512;
+            bulk_load(sf_base, sfa_src, (uint32_t)nsf * 512u, target, policy);
+            constexpr int B_BLOCKS = (BN_CTA + 127) / 128;
+#pragma unroll
+            for (int bb = 0; bb < B_BLOCKS; ++bb) {
+              const uint8_t* sfb_src = p.sfb + ((int64_t)(n0 / 128 + bb) * p.sf_kblocks + kq0) * 512;
+              bulk_load(sf_base + (uint32_t)nsf * 512u * (1 + bb), sfb_src, (uint32_t)nsf * 512u, target, policy);
+            }
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok && CG == 1) {
+        // Let every load already issued land before the CTA may exit.
+        for (int s = 0; s < p.stages; ++s)
+          if (issued_mask & (1u << s)) drain_wait(full_bar + 8u * s, (issued_parity >> s) & 1u, 100000000ull);
+      } else if (!ok) {
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {}
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int u = pair; u < p.num_units && ok; u += num_pairs) {
+        if (!wait_bar<CG == 2>(tempty_bar + 8u * acc, acc_phase ^ 1u, ctl, ROLE_MMA, 0x80u | acc)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!wait_bar<CG == 2>(full_bar + 8u * stage, phase, ctl, ROLE_MMA, stage)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sbase = ring + (uint32_t)stage * p.stage_bytes;
+          const uint32_t bbase = sbase + (uint32_t)p.atoms * p.a_atom_bytes;
+          if constexpr (DT == 2) {
+            // Copy this stage's scale factors into TMEM (columns after the
+            // two accumulators), then issue the block-scaled MMAs.
+            const uint32_t sf_base = bbase + (uint32_t)p.atoms * p.b_atom_bytes;
+            const int nsf = p.atoms * 4;
+            const uint32_t sfa_t = tmem_base + 2u * BN;
+            const uint32_t sfb_t = sfa_t + (uint32_t)nsf * SF_COLS_A;
+            for (int q = 0; q < nsf; ++q) {
+              tmem_cp_32x128b_warpx4<CG>(sfa_t + (uint32_t)q * SF_COLS_A, plain_desc(sf_base + (uint32_t)q * 512u));
+              for (int bb = 0; bb < SF_COLS_B / 4; ++bb)
+                tmem_cp_32x128b_warpx4<CG>(sfb_t + (uint32_t)q * SF_COLS_B + 4u * bb,
+                                           plain_desc(sf_base + (uint32_t)nsf * 512u * (1 + bb) + (uint32_t)q * 512u));
+            }
+            for (int ka = 0; ka < p.atoms; ++ka) {
+              const uint64_t ad = sw128_kmajor_desc(sbase + (uint32_t)ka * p.a_atom_bytes);
+              const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * p.b_atom_bytes);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const int q = ka * 4 + kk;
+                mma_nvf4<CG>(d_tmem, ad + 2u * kk, bd + 2u * kk, p.idesc,
+                             sfa_t + (uint32_t)q * SF_COLS_A, sfb_t + (uint32_t)q * SF_COLS_B,
+                             (kb | ka | kk) != 0);
+              }
+            }
+          } else {
+            for (int ka = 0; ka < p.atoms; ++ka) {
+              const uint64_t ad = sw128_kmajor_desc(sbase + (uint32_t)ka * p.a_atom_bytes);
+              const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * p.b_atom_bytes);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_ss<CG, KIND>(d_tmem, ad + 2u * kk, bd + 2u * kk, p.idesc, (kb | ka | kk) != 0);
+            }
+          }
+          issued = true;
+          if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3); else mma_commit(empty_bar + 8u * stage);
+          if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3); else mma_commit(tfull_bar + 8u * acc);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      if (!ok && issued) {
+        // Wait (bounded) until every MMA already issued has finished with TMEM.
+        if constexpr (CG == 2) mma_commit_pair(drain_bar, 0x1); else mma_commit(drain_bar);
+        drain_wait(drain_bar, 0, 100000000ull);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const uint32_t q = warp & 3u;                 // TMEM lane quadrant of this warp
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const uint32_t leader_tempty = CG == 2 ? mapa_shared(tempty_bar, 0) : tempty_bar;
+    for (int u = pair; u < p.num_units; u += num_pairs) {
+      int um, un;
+      unit_coords(u, p, um, un);
+      // Warp-uniform decision: tcgen05.ld below is warp-collective, so every
+      // lane must agree to proceed even if one lane saw an abort.
+      const bool ok = wait_bar<false>(tfull_bar + 8u * acc, acc_phase, ctl, ROLE_EPILOGUE, acc);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)um * MMA_M + (int64_t)cta_rank * BM + 32 * q + lane;
+      const int64_t n0 = (int64_t)un * BN;
+      const bool row_ok = row < p.m;
+      __nv_bfloat16* const dptr = p.d + row;
+      const uint32_t t_row = tmem_base + ((32u * q) << 16) + (uint32_t)(acc * BN);
+      if constexpr (BN % 32 == 0) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + (uint32_t)c, r);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int64_t col = n0 + c + j;
+              if (col < p.n) dptr[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(t_row + (uint32_t)c, r);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int64_t col = n0 + c + j;
+              if (col < p.n) dptr[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CG == 2) mbar_arrive_cluster(leader_tempty + 8u * acc); else mbar_arrive(tempty_bar + 8u * acc);
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  __syncwarp();
+  tc_fence_before();
+  if constexpr (CG == 2) { cluster_arrive(); cluster_wait(); } else { __syncthreads(); }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<CG>(tmem_base, (uint32_t)p.tmem_cols);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Host side
+// ----------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+
+struct Resolved {
+  int dt, cg, bm, bn, tile_k, atoms, stages, max_stages, cluster_m;
+  uint32_t a_atom_bytes, b_atom_bytes, sf_stage_bytes, stage_bytes;
+  int64_t smem_bytes;
+  int tmem_cols;
+  int num_m_units, num_n_units, num_units, num_k_blocks;
+  int grid, num_sms, raster_group;
+  char reason[128];
+};
+
+int next_pow2_cols(int c) {
+  int r = 32;
+  while (r < c) r <<= 1;
+  return r;
+}
+
+bool supported_bn(int cg, int bn) {
+  if (cg == 1) return bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 192 || bn == 256;
+  return bn == 64 || bn == 128 || bn == 192 || bn == 256;
+}
+
+#define FAIL(...) do { snprintf(r.reason, sizeof(r.reason), __VA_ARGS__); return GEMM_ERR_CANNOT_IMPLEMENT; } while (0)
+
+int resolve(const GemmArgs* a, Resolved& r) {
+  memset(&r, 0, sizeof(r));
+  if (!a) { snprintf(r.reason, sizeof(r.reason), "null args"); return GEMM_ERR_BAD_ARGS; }
+  if (a->struct_size != sizeof(GemmArgs)) {
+    snprintf(r.reason, sizeof(r.reason), "GemmArgs.struct_size %u != %zu", a->struct_size, sizeof(GemmArgs));
+    return GEMM_ERR_BAD_ARGS;
+  }
+  if (a->dtype < 0 || a->dtype > 2) FAIL("unknown dtype %d", a->dtype);
+  r.dt = a->dtype;
+  if (a->m <= 0 || a->n <= 0 || a->k <= 0) FAIL("empty problem %lld x %lld x %lld", (long long)a->m, (long long)a->n, (long long)a->k);
+  if (a->m > INT32_MAX / 2 || a->n > INT32_MAX / 2 || a->k > INT32_MAX / 2) FAIL("dimension too large");
+  if (!a->a || !a->b || !a->d) { snprintf(r.reason, sizeof(r.reason), "null A/B/D pointer"); return GEMM_ERR_BAD_ARGS; }
+  if (r.dt == 2 && (!a->sfa || !a->sfb)) { snprintf(r.reason, sizeof(r.reason), "NVFP4 needs sfa and sfb"); return GEMM_ERR_BAD_ARGS; }
+
+  r.cg = a->cta_group == 0 ? 1 : a->cta_group;
+  if (r.cg != 1 && r.cg != 2) FAIL("cta_group must be 1 or 2");
+  r.cluster_m = a->cluster_m == 0 ? r.cg : a->cluster_m;
+  if (r.cluster_m != r.cg) FAIL("cluster_m %d unsupported (must equal cta_group)", r.cluster_m);
+  r.bm = 128 * r.cg;
+  if (a->tile_m != 0 && a->tile_m != r.bm) FAIL("tile_m %d unsupported for cta_group %d (need %d)", a->tile_m, r.cg, r.bm);
+  r.bn = a->tile_n == 0 ? 256 : a->tile_n;
+  if (!supported_bn(r.cg, r.bn)) FAIL("tile_n %d unsupported for cta_group %d", r.bn, r.cg);
+  const int ae = atom_elems(r.dt);
+  r.tile_k = a->tile_k == 0 ? ae : a->tile_k;
+  if (r.tile_k % ae != 0) FAIL("tile_k %d must be a multiple of %d (one 128-byte swizzle atom)", r.tile_k, ae);
+  r.atoms = r.tile_k / ae;
+
+  // Element size in bytes (NVFP4: half a byte) and alignment (128-bit, as the reference's Alignment{A,B,D}).
+  const int64_t bits = r.dt == 0 ? 16 : (r.dt == 1 ? 8 : 4);
+  if (a->lda < a->k || a->ldb < a->k) FAIL("lda/ldb must be >= k");
+  if (a->ldd < a->m) FAIL("ldd must be >= m");
+  if ((a->lda * bits) % 128 != 0 || (a->ldb * bits) % 128 != 0) FAIL("lda/ldb rows must be 16-byte multiples");
+  if ((a->ldd * 16) % 128 != 0) FAIL("ldd must be a multiple of 8");
+  if (((uintptr_t)a->a | (uintptr_t)a->b | (uintptr_t)a->d) & 15) FAIL("A/B/D must be 16-byte aligned");
+  if ((a->k * bits) % 128 != 0) FAIL("k must be a multiple of %lld", (long long)(128 / bits));
+  if (r.dt == 2) {
+    if (r.cg != 1) FAIL("NVFP4 is implemented for cta_group 1 only");
+    if (a->k % r.tile_k != 0) FAIL("NVFP4 needs k %% tile_k == 0");
+    if (a->m % 128 != 0 || a->n % r.bn != 0) FAIL("NVFP4 needs m %% 128 == 0 and n %% tile_n == 0");
+    if (((uintptr_t)a->sfa | (uintptr_t)a->sfb) & 15) FAIL("sfa/sfb must be 16-byte aligned");
+  }
+
+  r.a_atom_bytes = 128u * 128u;
+  r.b_atom_bytes = (uint32_t)(r.bn / r.cg) * 128u;
+  r.sf_stage_bytes = 0;
+  if (r.dt == 2) {
+    const int b_blocks = (r.bn / r.cg + 127) / 128;
+    r.sf_stage_bytes = (uint32_t)(r.atoms * 4 * 512 * (1 + b_blocks));
+  }
+  r.stage_bytes = (uint32_t)r.atoms * (r.a_atom_bytes + r.b_atom_bytes) + r.sf_stage_bytes;
+  const int64_t fixed = 1024 /* alignment slack */ + kBarrierBytes;
+  r.max_stages = (int)((kSmemLimit - fixed) / r.stage_bytes);
+  if (r.max_stages > kMaxStages) r.max_stages = kMaxStages;
+  if (r.max_stages < 1) FAIL("one stage (%u B) exceeds shared memory", r.stage_bytes);
+  r.stages = a->stages == 0 ? r.max_stages : a->stages;
+  if (r.stages < 1) FAIL("stages must be >= 1");
+  if (r.stages > r.max_stages) FAIL("stages %d exceed shared memory (max %d at %u B/stage)", r.stages, r.max_stages, r.stage_bytes);
+  r.smem_bytes = fixed + (int64_t)r.stages * r.stage_bytes;
+
+  int cols = 2 * r.bn;
+  if (r.dt == 2) {
+    const int nsf = r.atoms * 4;
+    cols += nsf * 4 + nsf * ((r.bn + 127) / 128) * 4;
+  }
+  if (cols > 512) FAIL("TMEM: %d columns needed (2 accumulators + scales) > 512", cols);
+  r.tmem_cols = next_pow2_cols(cols);
+
+  r.num_m_units = (int)((a->m + r.bm - 1) / r.bm);
+  r.num_n_units = (int)((a->n + r.bn - 1) / r.bn);
+  r.num_units = r.num_m_units * r.num_n_units;
+  r.num_k_blocks = (int)((a->k + r.tile_k - 1) / r.tile_k);
+  r.raster_group = a->raster_group > 0 ? a->raster_group : 16;
+  if (r.raster_group > r.num_m_units) r.raster_group = r.num_m_units;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&r.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    r.num_sms = 148;
+    cudaGetLastError();
+  }
+  int pairs = r.num_sms / r.cg;
+  if (a->max_ctas > 0) pairs = a->max_ctas / r.cg > 0 ? a->max_ctas / r.cg : 1;
+  if (pairs > r.num_units) pairs = r.num_units;
+  r.grid = pairs * r.cg;
+  return GEMM_OK;
+}
+#undef FAIL
+
+bool encode_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType t, uint64_t inner, uint64_t outer,
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult res = g_encode(m, t, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return res == CUDA_SUCCESS;
+}
+
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, KernelParams);
+
+template <int DT, int CG, int BN>
+KernelFn kernel_ptr() { return gemm_sm100a_kernel<DT, CG, BN>; }
+
+template <int DT, int CG>
+KernelFn pick_bn(int bn) {
+  if constexpr (CG == 1) {
+    switch (bn) {
+      case 16: return kernel_ptr<DT, CG, 16>();
+      case 32: return kernel_ptr<DT, CG, 32>();
+      case 64: return kernel_ptr<DT, CG, 64>();
+      case 128: return kernel_ptr<DT, CG, 128>();
+      case 192: return kernel_ptr<DT, CG, 192>();
+      case 256: return kernel_ptr<DT, CG, 256>();
+    }
+  } else {
+    switch (bn) {
+      case 64: return kernel_ptr<DT, CG, 64>();
+      case 128: return kernel_ptr<DT, CG, 128>();
+      case 192: return kernel_ptr<DT, CG, 192>();
+      case 256: return kernel_ptr<DT, CG, 256>();
+    }
+  }
+  return nullptr;
+}
+
+KernelFn pick_kernel(int dt, int cg, int bn) {
+  switch (dt * 2 + (cg - 1)) {
+    case 0: return pick_bn<0, 1>(bn);
+    case 1: return pick_bn<0, 2>(bn);
+    case 2: return pick_bn<1, 1>(bn);
+    case 3: return pick_bn<1, 2>(bn);
+    case 4: return pick_bn<2, 1>(bn);
+    case 5: return pick_bn<2, 2>(bn);
+  }
+  return nullptr;
+}
+
+}  // namespace
+
+extern "C" int gemm_sm100a_query(const GemmArgs* args, GemmInfo* info) {
+  Resolved r;
+  const int rc = resolve(args, r);
+  if (info) {
+    memset(info, 0, sizeof(*info));
+    info->struct_size = sizeof(GemmInfo);
+    info->tile_m = r.bm; info->tile_n = r.bn; info->tile_k = r.tile_k; info->stages = r.stages;
+    info->cta_group = r.cg; info->cluster_m = r.cluster_m; info->max_stages = r.max_stages;
+    info->smem_bytes_per_stage = r.stage_bytes; info->smem_bytes = r.smem_bytes;
+    info->tmem_columns = r.tmem_cols; info->grid_ctas = r.grid; info->num_tiles = r.num_units;
+    info->num_sms = r.num_sms; info->can_implement = rc == GEMM_OK;
+    memcpy(info->reason, r.reason, sizeof(info->reason));
+  }
+  return rc;
+}
+
+extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
+  Resolved r;
+  int rc = resolve(args, r);
+  if (rc != GEMM_OK) return rc;
+  if (!get_encode()) return GEMM_ERR_LAUNCH;
+  const GemmArgs& a = *args;
+
+  CUtensorMap tma_a, tmb_b;
+  const bool bf = r.dt == 0;
+  const CUtensorMapDataType t = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const int64_t eb_num = r.dt == 0 ? 2 : 1, eb_den = r.dt == 2 ? 2 : 1;   // bytes per element = num/den
+  const uint64_t inner_k = (uint64_t)(r.dt == 2 ? a.k / 2 : a.k);       // tensor-map elements along K
+  const uint32_t box_inner = bf ? 64u : 128u;
+  if (!encode_2d(&tma_a, a.a, t, inner_k, (uint64_t)a.m, (uint64_t)(a.lda * eb_num / eb_den), box_inner, 128u))
+    return GEMM_ERR_CANNOT_IMPLEMENT;
+  if (!encode_2d(&tmb_b, a.b, t, inner_k, (uint64_t)a.n, (uint64_t)(a.ldb * eb_num / eb_den), box_inner,
+                 (uint32_t)(r.bn / r.cg)))
+    return GEMM_ERR_CANNOT_IMPLEMENT;
+
+  KernelParams p;
+  memset(&p, 0, sizeof(p));
+  p.m = (int32_t)a.m; p.n = (int32_t)a.n; p.k = (int32_t)a.k;
+  p.num_m_units = r.num_m_units; p.num_n_units = r.num_n_units; p.num_units = r.num_units;
+  p.num_k_blocks = r.num_k_blocks; p.atoms = r.atoms; p.stages = r.stages;
+  p.raster_group = r.raster_group; p.tmem_cols = r.tmem_cols;
+  p.stage_bytes = r.stage_bytes; p.a_atom_bytes = r.a_atom_bytes; p.b_atom_bytes = r.b_atom_bytes;
+  p.sf_stage_bytes = r.sf_stage_bytes;
+  p.idesc = make_idesc(r.dt, r.bm, r.bn);
+  p.alpha = a.alpha;
+  p.d = reinterpret_cast<__nv_bfloat16*>(a.d);
+  p.ldd = a.ldd;
+  p.status = a.status;
+  p.timeout_ns = (uint64_t)(a.timeout_ms ? a.timeout_ms : 4000u) * 1000000ull;
+  p.flags = a.flags;
+  p.sfa = reinterpret_cast<const uint8_t*>(a.sfa);
+  p.sfb = reinterpret_cast<const uint8_t*>(a.sfb);
+  p.sf_kblocks = (int32_t)(a.k / 64);
+
+  KernelFn fn = pick_kernel(r.dt, r.cg, r.bn);
+  if (!fn) return GEMM_ERR_CANNOT_IMPLEMENT;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r.smem_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return GEMM_ERR_LAUNCH;
+  }
+
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)r.grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)r.smem_bytes;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)r.cg;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tma_a, tmb_b, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return GEMM_ERR_LAUNCH;
+  }
+  return GEMM_OK;
+}
+
+extern "C" int gemm_sm100a_read_status(const int32_t* status, void* stream, int32_t* detail) {
+  if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) {
+    cudaGetLastError();
+    return GEMM_ERR_LAUNCH;
+  }
+  if (!status) { if (detail) *detail = 0; return GEMM_OK; }
+  int32_t v = 0;
+  if (cudaMemcpy(&v, status, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return GEMM_ERR_LAUNCH;
+  }
+  if (detail) *detail = v;
+  return v == 0 ? GEMM_OK : GEMM_ERR_TIMEOUT;
+}
+
+extern "C" const char* gemm_sm100a_strerror(int code) {
+  switch (code) {
+    case GEMM_OK: return "ok";
+    case GEMM_ERR_CANNOT_IMPLEMENT: return "cannot implement (shape, alignment, knob or shared-memory limit)";
+    case GEMM_ERR_LAUNCH: return "CUDA launch or driver error";
+    case GEMM_ERR_TIMEOUT: return "device wait timed out";
+    case GEMM_ERR_BAD_ARGS: return "bad arguments";
+  }
+  return "unknown error";
+}
+
+extern "C" int gemm_sm100a_version(void) { return 100; }
