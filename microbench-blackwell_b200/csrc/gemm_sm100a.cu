@@ -43,6 +43,7 @@ constexpr int kThreads = 192;
 constexpr int kSmemLimit = 232448;      // 227 KiB of opt-in dynamic shared memory per CTA
 constexpr int kBarrierBytes = 1024;     // barrier block + bookkeeping words
 constexpr int kMaxStages = 32;
+constexpr int kMinSmemPerCta = 120 * 1024;  // > half of the SM's 228 KiB: at most one CTA per SM
 
 enum Role : uint32_t { ROLE_PRODUCER = 1, ROLE_MMA = 2, ROLE_EPILOGUE = 3, ROLE_DRAIN = 4 };
 
@@ -513,6 +514,9 @@ int resolve(const GemmArgs* a, Resolved& r) {
   if (r.stages < 1) FAIL("stages must be >= 1");
   if (r.stages > r.max_stages) FAIL("stages %d exceed shared memory (max %d at %u B/stage)", r.stages, r.max_stages, r.stage_bytes);
   r.smem_bytes = fixed + (int64_t)r.stages * r.stage_bytes;
+  // One CTA per SM: the persistent schedule assumes it, and a second resident
+  // CTA would only stall in tcgen05.alloc until the first frees its columns.
+  if (r.smem_bytes < kMinSmemPerCta) r.smem_bytes = kMinSmemPerCta;
 
   int cols = 2 * r.bn;
   if (r.dt == 2) {
