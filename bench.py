@@ -225,10 +225,19 @@ def run_reference(args, wl, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def effective_knobs(wl, args) -> dict:
+    knobs = dict(wl["knobs"])
+    for key in ("stages", "tile_n", "tile_k", "cta_group"):
+        v = getattr(args, key, None)
+        if v is not None:
+            knobs[key] = v
+    return knobs
+
+
 def config_block(wl, world, args):
     return {"workload": args.workload, "baseline_config": wl["config"],
             "m": wl["m"], "n_per_gpu": wl["n"], "n_total": wl["n"] * world, "k": wl["k"],
-            "dtype": wl["dtype"], **{k: v for k, v in wl["knobs"].items()},
+            "dtype": wl["dtype"], **effective_knobs(wl, args),
             "parallelism": f"nsplit{world}" if world > 1 else "single",
             "layout": "A row-major MxK, B NxK (K-major), D column-major bf16",
             "l2": "inputs larger than L2 (126 MB), no flush" if wl["m"] * wl["k"] * elem_bytes(wl["dtype"]) +
@@ -246,11 +255,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     st = stream.cuda_stream
     dt = dtype_code(pkg, wl["dtype"])
     m, n, k = wl["m"], wl["n"], wl["k"]
-    knobs = dict(wl["knobs"])
-    if args.stages is not None:
-        knobs["stages"] = args.stages
-    if args.tile_n is not None:
-        knobs["tile_n"] = args.tile_n
+    knobs = effective_knobs(wl, args)
     n0 = rank * n
     with torch.cuda.stream(stream):
         ops = pkg.make_operands(dt, m, n, k, seed=args.seed,
@@ -436,6 +441,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bf16_8192")
     ap.add_argument("--stages", type=int, default=None)
     ap.add_argument("--tile-n", type=int, default=None)
+    ap.add_argument("--tile-k", type=int, default=None)
+    ap.add_argument("--cta-group", type=int, default=None, choices=[1, 2])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

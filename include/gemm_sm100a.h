@@ -100,6 +100,7 @@ typedef struct GemmArgs {
   int32_t* status;        /* optional device int32: 0 on success, GEMM_ERR_TIMEOUT (and where) on a device wait timeout */
   uint32_t timeout_ms;    /* device wait budget; 0 = default (4000 ms) */
   uint32_t flags;         /* GEMM_FLAG_* */
+  int32_t  l2_prefetch;   /* warm L2 this many k-blocks ahead of the shared-memory ring; 0 = default, < 0 = off */
 } GemmArgs;
 
 /* What a launch would do; filled by gemm_sm100a_query. */

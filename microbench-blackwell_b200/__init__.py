@@ -44,6 +44,7 @@ class GemmArgs(C.Structure):
         ("cta_group", C.c_int32), ("cluster_m", C.c_int32), ("max_ctas", C.c_int32),
         ("raster_group", C.c_int32),
         ("status", C.c_void_p), ("timeout_ms", C.c_uint32), ("flags", C.c_uint32),
+        ("l2_prefetch", C.c_int32),
     ]
 
 
@@ -114,7 +115,8 @@ def make_args(*, dtype: int, m: int, n: int, k: int, a: int, b: int, d: int,
               sfa: int | None = None, sfb: int | None = None, alpha: float = 1.0,
               tile_m: int = 0, tile_n: int = 0, tile_k: int = 0, stages: int = 0,
               cta_group: int = 0, cluster_m: int = 0, max_ctas: int = 0, raster_group: int = 0,
-              status: int | None = None, timeout_ms: int = 0, flags: int = 0) -> GemmArgs:
+              status: int | None = None, timeout_ms: int = 0, flags: int = 0,
+              l2_prefetch: int = 0) -> GemmArgs:
     """GemmArgs from raw device addresses (ints).  Leading dimensions default to packed."""
     g = GemmArgs()
     g.struct_size = C.sizeof(GemmArgs)
@@ -129,6 +131,7 @@ def make_args(*, dtype: int, m: int, n: int, k: int, a: int, b: int, d: int,
     g.cta_group, g.cluster_m, g.max_ctas, g.raster_group = cta_group, cluster_m, max_ctas, raster_group
     g.status = status
     g.timeout_ms, g.flags = timeout_ms, flags
+    g.l2_prefetch = l2_prefetch
     return g
 
 

@@ -39,10 +39,13 @@ using namespace sm100;
 
 namespace {
 
-constexpr int kThreads = 192;
+// Threads per CTA: producer warp + MMA warp + EPI_WARPS epilogue warps.
+__host__ __device__ constexpr int epi_warps_for(int bn) { return bn > 256 ? 8 : 4; }
+__host__ __device__ constexpr int threads_for(int bn) { return 64 + 32 * epi_warps_for(bn); }
 constexpr int kSmemLimit = 232448;      // 227 KiB of opt-in dynamic shared memory per CTA
 constexpr int kBarrierBytes = 1024;     // barrier block + bookkeeping words
 constexpr int kMaxStages = 32;
+constexpr int kDefaultL2Prefetch = 0;         // k-blocks of L2 prefetch ahead of the ring (0 = off)
 constexpr int kMinSmemPerCta = 120 * 1024;  // > half of the SM's 228 KiB: at most one CTA per SM
 
 enum Role : uint32_t { ROLE_PRODUCER = 1, ROLE_MMA = 2, ROLE_EPILOGUE = 3, ROLE_DRAIN = 4 };
@@ -68,6 +71,8 @@ struct KernelParams {
   const uint8_t* sfa;
   const uint8_t* sfb;
   int32_t sf_kblocks;     // K / 64 (NVFP4 scale atoms along K)
+  int32_t l2_prefetch;    // k-blocks the L2 prefetch cursor runs ahead of the loads (0 = off)
+  int32_t num_acc;        // accumulator buffers in TMEM (2 = epilogue overlaps the next tile)
 };
 
 // Elements of each dtype in one 128-byte swizzle atom row.
@@ -115,19 +120,27 @@ __device__ __noinline__ void raise_abort(const SharedCtl& c, uint32_t role, uint
 }
 
 // Bounded wait for phase `parity` of mbarrier `bar`; false when aborted.
+// Each probe lets the hardware suspend the thread until the phase completes
+// (or kWaitHintNs passes), so a completed phase is noticed at once; the
+// abort flag is checked after every probe and the timer every 8 probes.
+constexpr uint32_t kWaitHintNs = 200000;
 template <bool kCluster>
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const SharedCtl& c,
                                          uint32_t role, uint32_t idx) {
   if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i)
-      if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = 0;
+  for (uint32_t probe = 1;; ++probe) {
+    if (kCluster ? mbar_try_wait_cluster_hint(bar, parity, kWaitHintNs) : mbar_try_wait_hint(bar, parity, kWaitHintNs))
+      return true;
     if (ld_shared_volatile_u32(c.abort_addr)) return false;
-    if (globaltimer_ns() - t0 > c.timeout_ns) {
-      raise_abort(c, role, idx);
-      return false;
+    if ((probe & 7u) == 1u) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > c.timeout_ns) {
+        raise_abort(c, role, idx);
+        return false;
+      }
     }
   }
 }
@@ -156,12 +169,16 @@ __device__ __forceinline__ void unit_coords(int u, const KernelParams& p, int& u
 // (the pair's full N for CG = 2; each CTA of the pair loads BN / 2 rows of B).
 // ----------------------------------------------------------------------------
 template <int DT, int CG, int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for(BN), 1)
 gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ KernelParams p) {
   constexpr int BM = 128;                 // A rows per CTA (= TMEM lanes)
   constexpr int BN_CTA = BN / CG;         // B rows per CTA
+  constexpr int MMA_N = BN > 256 ? 256 : BN;  // N of one tcgen05.mma
+  constexpr int N_SUB = BN / MMA_N;       // MMAs per K step (N halves of a 512-wide pair tile)
+  constexpr int B_BOX = MMA_N / CG;       // B rows per CTA per N half (one TMA box)
+  constexpr int EPI_WARPS = epi_warps_for(BN);
   constexpr int MMA_M = BM * CG;
   constexpr int KIND = DT == 0 ? 0 : 1;
   constexpr int MAP_ELEMS_PER_ATOM = DT == 0 ? 64 : 128;  // tensor-map elements per 128 B
@@ -200,7 +217,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar + 8u * a, 1);
-      mbar_init(tempty_bar + 8u * a, 4 * CG);   // one arrive per epilogue warp of the pair
+      mbar_init(tempty_bar + 8u * a, EPI_WARPS * CG);   // one arrive per epilogue warp of the pair
     }
     mbar_init(drain_bar, 1);
     st_shared_u32(abort_flag, 0u);
@@ -231,13 +248,41 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
+      // L2 prefetch cursor: runs p.l2_prefetch k-blocks ahead of the load
+      // cursor over the same (unit, k-block) sequence.
+      int pf_u = pair, pf_kb = 0, pf_m0 = 0, pf_n0 = 0;
+      auto pf_coords = [&]() {
+        int um, un;
+        unit_coords(pf_u, p, um, un);
+        pf_m0 = um * MMA_M + (int32_t)cta_rank * BM;
+        pf_n0 = un * BN + (int32_t)cta_rank * B_BOX;
+      };
+      auto pf_step = [&]() {
+        if (pf_u >= p.num_units) return;
+        for (int ka = 0; ka < p.atoms; ++ka) {
+          const int32_t x = (pf_kb * p.atoms + ka) * MAP_ELEMS_PER_ATOM;
+          tma_prefetch_l2_2d(&tmap_a, x, pf_m0);
+#pragma unroll
+          for (int h = 0; h < N_SUB; ++h) tma_prefetch_l2_2d(&tmap_b, x, pf_n0 + h * MMA_N);
+        }
+        if (++pf_kb == p.num_k_blocks) {
+          pf_kb = 0;
+          pf_u += num_pairs;
+          if (pf_u < p.num_units) pf_coords();
+        }
+      };
+      if (p.l2_prefetch > 0 && pf_u < p.num_units) {
+        pf_coords();
+        for (int i = 0; i < p.l2_prefetch; ++i) pf_step();
+      }
       for (int u = pair; u < p.num_units && ok; u += num_pairs) {
         int um, un;
         unit_coords(u, p, um, un);
         const int32_t m0 = um * MMA_M + (int32_t)cta_rank * BM;
-        const int32_t n0 = un * BN + (int32_t)cta_rank * BN_CTA;
+        const int32_t n0 = un * BN + (int32_t)cta_rank * B_BOX;
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!wait_bar<false>(empty_bar + 8u * stage, phase ^ 1u, ctl, ROLE_PRODUCER, stage)) { ok = false; break; }
+          if (p.l2_prefetch > 0) pf_step();
           const uint32_t sbase = ring + (uint32_t)stage * p.stage_bytes;
           const uint32_t fb = full_bar + 8u * stage;
           if (leader) mbar_arrive_expect_tx(fb, tx_bytes);
@@ -248,10 +293,14 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t b_dst = sbase + (uint32_t)p.atoms * p.a_atom_bytes + (uint32_t)ka * p.b_atom_bytes;
             if constexpr (CG == 2) {
               tma_load_2d_pair(a_dst, &tmap_a, target, x, m0, policy);
-              tma_load_2d_pair(b_dst, &tmap_b, target, x, n0, policy);
+#pragma unroll
+              for (int h = 0; h < N_SUB; ++h)
+                tma_load_2d_pair(b_dst + (uint32_t)(h * B_BOX * 128), &tmap_b, target, x, n0 + h * MMA_N, policy);
             } else {
               tma_load_2d(a_dst, &tmap_a, target, x, m0, policy);
-              tma_load_2d(b_dst, &tmap_b, target, x, n0, policy);
+#pragma unroll
+              for (int h = 0; h < N_SUB; ++h)
+                tma_load_2d(b_dst + (uint32_t)(h * B_BOX * 128), &tmap_b, target, x, n0 + h * MMA_N, policy);
             }
           }
           if constexpr (DT == 2) {
@@ -307,7 +356,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
             // two accumulators), then issue the block-scaled MMAs.
             const uint32_t sf_base = bbase + (uint32_t)p.atoms * p.b_atom_bytes;
             const int nsf = p.atoms * 4;
-            const uint32_t sfa_t = tmem_base + 2u * BN;
+            const uint32_t sfa_t = tmem_base + (uint32_t)(p.num_acc * BN);
             const uint32_t sfb_t = sfa_t + (uint32_t)nsf * SF_COLS_A;
             for (int q = 0; q < nsf; ++q) {
               tmem_cp_32x128b_warpx4<CG>(sfa_t + (uint32_t)q * SF_COLS_A, plain_desc(sf_base + (uint32_t)q * 512u));
@@ -332,7 +381,10 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
               const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * p.b_atom_bytes);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
-                mma_ss<CG, KIND>(d_tmem, ad + 2u * kk, bd + 2u * kk, p.idesc, (kb | ka | kk) != 0);
+#pragma unroll
+                for (int h = 0; h < N_SUB; ++h)
+                  mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
+                                   bd + (uint64_t)((h * B_BOX * 128) >> 4) + 2u * kk, p.idesc, (kb | ka | kk) != 0);
             }
           }
           issued = true;
@@ -341,7 +393,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
         if (!ok) break;
         if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3); else mma_commit(tfull_bar + 8u * acc);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        if (++acc == p.num_acc) { acc = 0; acc_phase ^= 1u; }
       }
       if (!ok && issued) {
         // Wait (bounded) until every MMA already issued has finished with TMEM.
@@ -352,6 +404,8 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   } else {
     // ------------------------------------------------------------ epilogue
     const uint32_t q = warp & 3u;                 // TMEM lane quadrant of this warp
+    constexpr int COLS = BN / (EPI_WARPS / 4);    // accumulator columns per epilogue warp
+    const int c_begin = (int)((warp - 2u) / 4u) * COLS;
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t leader_tempty = CG == 2 ? mapa_shared(tempty_bar, 0) : tempty_bar;
@@ -368,9 +422,9 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const bool row_ok = row < p.m;
       __nv_bfloat16* const dptr = p.d + row;
       const uint32_t t_row = tmem_base + ((32u * q) << 16) + (uint32_t)(acc * BN);
-      if constexpr (BN % 32 == 0) {
+      if constexpr (COLS % 32 == 0) {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = c_begin; c < c_begin + COLS; c += 32) {
           uint32_t r[32];
           tmem_ld32(t_row + (uint32_t)c, r);
           tmem_ld_wait();
@@ -384,7 +438,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = c_begin; c < c_begin + COLS; c += 16) {
           uint32_t r[16];
           tmem_ld16(t_row + (uint32_t)c, r);
           tmem_ld_wait();
@@ -402,7 +456,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (lane == 0) {
         if constexpr (CG == 2) mbar_arrive_cluster(leader_tempty + 8u * acc); else mbar_arrive(tempty_bar + 8u * acc);
       }
-      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      if (++acc == p.num_acc) { acc = 0; acc_phase ^= 1u; }
     }
   }
 
@@ -437,7 +491,7 @@ struct Resolved {
   int dt, cg, bm, bn, tile_k, atoms, stages, max_stages, cluster_m;
   uint32_t a_atom_bytes, b_atom_bytes, sf_stage_bytes, stage_bytes;
   int64_t smem_bytes;
-  int tmem_cols;
+  int tmem_cols, num_acc, threads;
   int num_m_units, num_n_units, num_units, num_k_blocks;
   int grid, num_sms, raster_group;
   char reason[128];
@@ -451,7 +505,7 @@ int next_pow2_cols(int c) {
 
 bool supported_bn(int cg, int bn) {
   if (cg == 1) return bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 192 || bn == 256;
-  return bn == 64 || bn == 128 || bn == 192 || bn == 256;
+  return bn == 64 || bn == 128 || bn == 192 || bn == 256 || bn == 512;
 }
 
 #define FAIL(...) do { snprintf(r.reason, sizeof(r.reason), __VA_ARGS__); return GEMM_ERR_CANNOT_IMPLEMENT; } while (0)
@@ -518,13 +572,18 @@ int resolve(const GemmArgs* a, Resolved& r) {
   // CTA would only stall in tcgen05.alloc until the first frees its columns.
   if (r.smem_bytes < kMinSmemPerCta) r.smem_bytes = kMinSmemPerCta;
 
-  int cols = 2 * r.bn;
+  int sf_cols = 0;
   if (r.dt == 2) {
     const int nsf = r.atoms * 4;
-    cols += nsf * 4 + nsf * ((r.bn + 127) / 128) * 4;
+    sf_cols = nsf * 4 + nsf * ((r.bn + 127) / 128) * 4;
   }
-  if (cols > 512) FAIL("TMEM: %d columns needed (2 accumulators + scales) > 512", cols);
+  // Two accumulator buffers when they fit (the epilogue then overlaps the
+  // next tile's mainloop), else one.
+  r.num_acc = 2 * r.bn + sf_cols <= 512 ? 2 : 1;
+  const int cols = r.num_acc * r.bn + sf_cols;
+  if (cols > 512) FAIL("TMEM: %d columns needed (accumulator + scales) > 512", cols);
   r.tmem_cols = next_pow2_cols(cols);
+  r.threads = threads_for(r.bn);
 
   r.num_m_units = (int)((a->m + r.bm - 1) / r.bm);
   r.num_n_units = (int)((a->n + r.bn - 1) / r.bn);
@@ -581,6 +640,9 @@ KernelFn pick_bn(int bn) {
       case 128: return kernel_ptr<DT, CG, 128>();
       case 192: return kernel_ptr<DT, CG, 192>();
       case 256: return kernel_ptr<DT, CG, 256>();
+      case 512:
+        if constexpr (DT != 2) return kernel_ptr<DT, CG, 512>();
+        break;
     }
   }
   return nullptr;
@@ -632,7 +694,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   if (!encode_2d(&tma_a, a.a, t, inner_k, (uint64_t)a.m, (uint64_t)(a.lda * eb_num / eb_den), box_inner, 128u))
     return GEMM_ERR_CANNOT_IMPLEMENT;
   if (!encode_2d(&tmb_b, a.b, t, inner_k, (uint64_t)a.n, (uint64_t)(a.ldb * eb_num / eb_den), box_inner,
-                 (uint32_t)(r.bn / r.cg)))
+                 (uint32_t)((r.bn > 256 ? 256 : r.bn) / r.cg)))
     return GEMM_ERR_CANNOT_IMPLEMENT;
 
   KernelParams p;
@@ -643,7 +705,8 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   p.raster_group = r.raster_group; p.tmem_cols = r.tmem_cols;
   p.stage_bytes = r.stage_bytes; p.a_atom_bytes = r.a_atom_bytes; p.b_atom_bytes = r.b_atom_bytes;
   p.sf_stage_bytes = r.sf_stage_bytes;
-  p.idesc = make_idesc(r.dt, r.bm, r.bn);
+  p.idesc = make_idesc(r.dt, r.bm, r.bn > 256 ? 256 : r.bn);
+  p.num_acc = r.num_acc;
   p.alpha = a.alpha;
   p.d = reinterpret_cast<__nv_bfloat16*>(a.d);
   p.ldd = a.ldd;
@@ -653,6 +716,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   p.sfa = reinterpret_cast<const uint8_t*>(a.sfa);
   p.sfb = reinterpret_cast<const uint8_t*>(a.sfb);
   p.sf_kblocks = (int32_t)(a.k / 64);
+  p.l2_prefetch = a.l2_prefetch < 0 ? 0 : (a.l2_prefetch == 0 ? kDefaultL2Prefetch : a.l2_prefetch);
 
   KernelFn fn = pick_kernel(r.dt, r.cg, r.bn);
   if (!fn) return GEMM_ERR_CANNOT_IMPLEMENT;
@@ -664,7 +728,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)r.grid, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3((unsigned)r.threads, 1, 1);
   cfg.dynamicSmemBytes = (size_t)r.smem_bytes;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
