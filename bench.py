@@ -39,10 +39,13 @@ REF_SINGLE_CTA_TFLOPS = {"bf16": 10.4596, "e4m3": 20.6377}  # cutlass_gemm_mainl
 WORKLOADS = {
     # name: dtype, M, N (per GPU), K, knobs, inputs
     "bf16_8192": dict(dtype="bf16", m=8192, n=8192, k=8192,
-                      knobs=dict(tile_n=256, tile_k=64, stages=4, cta_group=1),
+                      knobs=dict(tile_n=512, tile_k=64, stages=0, cta_group=2, raster_group=1),
                       a=("uniform", 1.0), b=("uniform", 1.0), config=2),
+    "bf16_8192_1sm": dict(dtype="bf16", m=8192, n=8192, k=8192,
+                          knobs=dict(tile_n=256, tile_k=64, stages=4, cta_group=1, raster_group=1),
+                          a=("uniform", 1.0), b=("uniform", 1.0), config=2),
     "e4m3_16384_2sm": dict(dtype="e4m3", m=16384, n=16384, k=16384,
-                           knobs=dict(tile_n=256, tile_k=128, stages=0, cta_group=2),
+                           knobs=dict(tile_n=512, tile_k=128, stages=0, cta_group=2, raster_group=16),
                            a=("normal", 0.25), b=("normal", 0.25), config=3),
     "nvfp4_mlp": dict(dtype="nvfp4", m=8192, n=28672, k=8192,
                       knobs=dict(tile_n=192, tile_k=256, stages=0, cta_group=1),
@@ -227,7 +230,7 @@ def run_reference(args, wl, rank: int, world: int):
 
 def effective_knobs(wl, args) -> dict:
     knobs = dict(wl["knobs"])
-    for key in ("stages", "tile_n", "tile_k", "cta_group"):
+    for key in ("stages", "tile_n", "tile_k", "cta_group", "raster_group"):
         v = getattr(args, key, None)
         if v is not None:
             knobs[key] = v
@@ -443,6 +446,7 @@ def main():
     ap.add_argument("--tile-n", type=int, default=None)
     ap.add_argument("--tile-k", type=int, default=None)
     ap.add_argument("--cta-group", type=int, default=None, choices=[1, 2])
+    ap.add_argument("--raster-group", type=int, default=None)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

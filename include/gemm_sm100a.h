@@ -96,7 +96,7 @@ typedef struct GemmArgs {
   int32_t  cta_group;     /* 1 or 2; 0 = default (1) */
   int32_t  cluster_m;     /* CTAs per cluster along M; 0 = cta_group */
   int32_t  max_ctas;      /* grid cap; 0 = one CTA per SM (persistent); 1 = single-CTA mainloop mode */
-  int32_t  raster_group;  /* M tiles per rasterisation group (L2 locality); 0 = default */
+  int32_t  raster_group;  /* tile order for L2 reuse: G > 0 groups of G M-tiles (M fastest), G < 0 groups of -G N-tiles (N fastest); 0 = default */
   int32_t* status;        /* optional device int32: 0 on success, GEMM_ERR_TIMEOUT (and where) on a device wait timeout */
   uint32_t timeout_ms;    /* device wait budget; 0 = default (4000 ms) */
   uint32_t flags;         /* GEMM_FLAG_* */

@@ -153,15 +153,29 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, uint64
   }
 }
 
+// Output-tile rasterisation.  raster_group G > 0: groups of G M-tiles, M
+// fastest inside a group (tiles sharing B run together); G < 0: groups of |G|
+// N-tiles, N fastest (tiles sharing A run together).
 __device__ __forceinline__ void unit_coords(int u, const KernelParams& p, int& um, int& un) {
-  const int G = p.raster_group;
-  const int per_group = G * p.num_n_units;
-  const int g = u / per_group;
-  const int first_m = g * G;
-  const int rows = min(p.num_m_units - first_m, G);
-  const int r = u - g * per_group;
-  um = first_m + r % rows;
-  un = r / rows;
+  if (p.raster_group > 0) {
+    const int G = p.raster_group;
+    const int per_group = G * p.num_n_units;
+    const int g = u / per_group;
+    const int first_m = g * G;
+    const int rows = min(p.num_m_units - first_m, G);
+    const int r = u - g * per_group;
+    um = first_m + r % rows;
+    un = r / rows;
+  } else {
+    const int G = -p.raster_group;
+    const int per_group = G * p.num_m_units;
+    const int g = u / per_group;
+    const int first_n = g * G;
+    const int cols = min(p.num_n_units - first_n, G);
+    const int r = u - g * per_group;
+    un = first_n + r % cols;
+    um = r / cols;
+  }
 }
 
 // ----------------------------------------------------------------------------
@@ -589,8 +603,9 @@ int resolve(const GemmArgs* a, Resolved& r) {
   r.num_n_units = (int)((a->n + r.bn - 1) / r.bn);
   r.num_units = r.num_m_units * r.num_n_units;
   r.num_k_blocks = (int)((a->k + r.tile_k - 1) / r.tile_k);
-  r.raster_group = a->raster_group > 0 ? a->raster_group : 16;
+  r.raster_group = a->raster_group != 0 ? a->raster_group : 1;
   if (r.raster_group > r.num_m_units) r.raster_group = r.num_m_units;
+  if (-r.raster_group > r.num_n_units) r.raster_group = -r.num_n_units;
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
