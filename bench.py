@@ -162,37 +162,66 @@ def elem_bytes(name: str) -> float:
     return {"bf16": 2.0, "e4m3": 1.0, "nvfp4": 0.5}[name]
 
 
-def cpu_gemm_sample(wl: dict, budget_s: float, seed: int = 0):
-    """Time the oracle's OpenMP GEMM on a slab of rows of A against all of B (dequantised fp32)."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
-    import oracle as O
-    m, n, k, dt = wl["m"], wl["n"], wl["k"], wl["dtype"]
-    # B is the large operand; limit it to at most 8192 rows so setup stays bounded.
-    nb = min(n, 8192)
-    if dt == "nvfp4":
-        pb, sb = O.generate_nvfp4(nb, k, wl["b"][1], seed, 1)
-        B = O.dequant_nvfp4(pb, sb, k)
-    else:
-        odt = O.BF16 if dt == "bf16" else O.FP8_E4M3
-        B = O.dequant(O.generate(nb, k, odt, 0 if wl["b"][0] == "uniform" else 1, wl["b"][1], seed, 1), odt)
-    rows = 16
-    while True:
+class CpuGemm:
+    """The oracle's OpenMP fp32-accumulate GEMM (oracle/cpu_gemm.c) on a slab of
+    rows of A against B (dequantised fp32).  B is capped at 8192 rows so set-up
+    stays bounded; the slab height is chosen once so one timed call takes
+    about `target_s` seconds."""
+
+    def __init__(self, wl: dict, seed: int = 0, target_s: float = 1.0):
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as O
+        self.O = O
+        m, n, k, dt = wl["m"], wl["n"], wl["k"], wl["dtype"]
+        self.m, self.k, self.dt = m, k, dt
+        self.nb = min(n, 8192)
+        self.wl = wl
+        rows_max = min(m, 1024)
         if dt == "nvfp4":
-            pa, sa = O.generate_nvfp4(max(rows, 128), k, wl["a"][1], seed, 0)
-            A = O.dequant_nvfp4(pa, sa, k)[:rows]
+            pb, sb = O.generate_nvfp4(self.nb, k, wl["b"][1], seed, 1)
+            self.B = O.dequant_nvfp4(pb, sb, k)
+            pa, sa = O.generate_nvfp4(max(128, (rows_max + 127) // 128 * 128), k, wl["a"][1], seed, 0)
+            self.A = O.dequant_nvfp4(pa, sa, k)[:rows_max]
         else:
-            A = O.dequant(O.generate(rows, k, odt, 0 if wl["a"][0] == "uniform" else 1, wl["a"][1], seed, 0), odt)
+            odt = O.BF16 if dt == "bf16" else O.FP8_E4M3
+            self.B = O.dequant(O.generate(self.nb, k, odt, 0 if wl["b"][0] == "uniform" else 1, wl["b"][1], seed, 1), odt)
+            self.A = O.dequant(O.generate(rows_max, k, odt, 0 if wl["a"][0] == "uniform" else 1, wl["a"][1], seed, 0), odt)
+        rows = 16
+        while True:
+            t = self._time(rows)
+            if t * 2 > target_s or rows >= rows_max:
+                break
+            rows = min(rows_max, rows * 2)
+        self.rows = rows
+
+    def _time(self, rows: int) -> float:
+        import numpy as np
+        A = np.ascontiguousarray(self.A[:rows])
         t0 = time.perf_counter()
-        O.gemm_omp_f32(A, B)
-        dt_s = time.perf_counter() - t0
-        if dt_s * 4 > budget_s or rows >= m:
-            break
-        rows = min(m, rows * 4)
-    flops = 2.0 * rows * nb * k
-    return {"value": flops / dt_s / 1e12, "unit": "TFLOPS", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{rows} x {nb} x {k} slab of the {m}x{n}x{k} {dt} GEMM "
-                      f"(oracle/cpu_gemm.c OpenMP fp32-accumulate over dequantised inputs), {dt_s:.2f} s"}, dt_s
+        self.O.gemm_omp_f32(A, self.B)
+        return time.perf_counter() - t0
+
+    def step(self) -> float:
+        """TFLOPS of one timed slab."""
+        t = self._time(self.rows)
+        return 2.0 * self.rows * self.nb * self.k / t / 1e12
+
+    def describe(self, secs: float) -> dict:
+        return {"unit": "TFLOPS", "cores": self.O.num_threads(), "kind": "port",
+                "sample": f"{self.rows} x {self.nb} x {self.k} row slab of the {self.m}x{self.wl['n']}x{self.k} "
+                          f"{self.dt} GEMM (oracle/cpu_gemm.c, OpenMP fp32 accumulate over dequantised inputs), "
+                          f"{secs:.1f} s of timed CPU work"}
+
+
+def cpu_gemm_sample(wl: dict, budget_s: float, seed: int = 0):
+    g = CpuGemm(wl, seed=seed, target_s=1.0)
+    vals = []
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or not vals:
+        vals.append(g.step())
+    info = g.describe(time.perf_counter() - t0)
+    info["value"] = statistics.median(vals)
+    return info, time.perf_counter() - t0
 
 
 def host_note_cores() -> int:
@@ -206,15 +235,15 @@ def host_note_cores() -> int:
 def run_reference(args, wl, rank: int, world: int):
     if rank != 0:
         return
-    budget = 8.0
+    g = CpuGemm(wl, seed=args.seed, target_s=1.0)
     per_step = []
-    info = None
+    t0 = time.perf_counter()
     for i in range(args.warmup + args.steps):
-        cb, secs = cpu_gemm_sample(wl, budget_s=budget / 4)
+        v = g.step()
         if i >= args.warmup:
-            per_step.append(cb["value"])
-        info = cb
+            per_step.append(v)
     value = statistics.median(per_step)
+    info = g.describe(time.perf_counter() - t0)
     info["value"] = value
     line = {"metric": "GEMM TFLOPS", "impl": "reference", "value": value, "unit": "TFLOPS",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -223,6 +252,7 @@ def run_reference(args, wl, rank: int, world: int):
             "config": config_block(wl, world, args),
             "cpu_baseline": info,
             "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "reference_cutlass_single_cta": run_reference_cutlass_single_cta(wl),
             "note": "the reference has no CPU GEMM; this arm times oracle/cpu_gemm.c (OpenMP host GEMM) "
                     "on a row slab, host cores only"}
     print(json.dumps(line), flush=True)
@@ -322,7 +352,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     e2e = run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank)
 
     # ---------------------------------------------------------- single-CTA mainloop (reference experiment)
-    single = run_single_cta(pkg, wl, dev, stream) if (rank == 0 and wl["dtype"] in REF_SINGLE_CTA_TFLOPS) else None
+    single = run_single_cta(pkg, wl, dev, stream) if (rank == 0 and wl["dtype"] in SINGLE_CTA_CFG) else None
 
     if rank != 0:
         return
@@ -407,32 +437,55 @@ def run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank):
             "path": "pinned host A,B -> gemm_sm100a_launch -> pinned host D, one stream"}
 
 
+SINGLE_CTA_CFG = {"bf16": (128, 256, 64, 4, 0), "e4m3": (128, 256, 128, 0, 1)}
+
+
+def parse_csv_line(text: str):
+    line = [l for l in text.strip().splitlines() if l and not l.startswith("#")][-1]
+    f = line.split(",")
+    return {"M": int(f[0]), "N": int(f[1]), "K": int(f[2]), "tile": [int(f[3]), int(f[4]), int(f[5])],
+            "stages": int(f[6]), "dtype": f[7], "time_ms": float(f[8]), "tflops": float(f[9])}
+
+
 def run_single_cta(pkg, wl, dev, stream):
-    """The reference experiment: one CTA, M=TILE_M, N=TILE_N, K=131072, 1 warm-up + 20 timed
-    (cutlass_gemm_bench.cu:158-257).  Inputs are seeded (the reference zero-fills)."""
-    import torch
-    dt = dtype_code(pkg, wl["dtype"])
-    tn = 256
-    tk = 64 if wl["dtype"] == "bf16" else 128
-    K = 131072
-    ops = pkg.make_operands(dt, 128, tn, K, seed=1, device=dev, stream=stream.cuda_stream)
-    g = pkg.make_args(dtype=dt, m=128, n=tn, k=K, a=ops.a.data_ptr(), b=ops.b.data_ptr(), d=ops.d.data_ptr(),
-                      tile_n=tn, tile_k=tk, stages=4, max_ctas=1)
-    L = pkg.lib()
-    sp = C.c_void_p(stream.cuda_stream)
-    L.gemm_sm100a_launch(C.byref(g), sp)
-    stream.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for _ in range(20):
-        L.gemm_sm100a_launch(C.byref(g), sp)
-    e.record(stream)
-    e.synchronize()
-    ms = s.elapsed_time(e) / 20
-    tf = 2.0 * 128 * tn * K / (ms * 1e-3) / 1e12
-    return {"tile": [128, tn, tk], "stages": 4, "k": K, "time_ms": ms, "tflops": tf,
-            "reference_published_tflops": REF_SINGLE_CTA_TFLOPS[wl["dtype"]],
-            "ratio_vs_reference": tf / REF_SINGLE_CTA_TFLOPS[wl["dtype"]]}
+    """The reference experiment through our drop-in harness binary, run exactly as
+    the reference runs its own: no argv, one CTA, M=TILE_M, N=TILE_N, K=131072,
+    zero-filled inputs, 1 warm-up + 20 timed (cutlass_gemm_bench.cu:158-257)."""
+    import subprocess
+    cfg = SINGLE_CTA_CFG[wl["dtype"]]
+    binp = PKG_DIR / "harness" / "bin" / ("gemm_bench_%d_%d_%d_s%d_d%d" % cfg)
+    if not binp.exists():
+        return {"error": f"{binp.name} not built"}
+    r = subprocess.run([str(binp)], capture_output=True, text=True, timeout=120)
+    if r.returncode != 0:
+        return {"error": r.stderr.strip()[-200:]}
+    out = parse_csv_line(r.stdout)
+    out["reference_published_tflops"] = REF_SINGLE_CTA_TFLOPS[wl["dtype"]]
+    out["ratio_vs_published"] = out["tflops"] / REF_SINGLE_CTA_TFLOPS[wl["dtype"]]
+    out["binary"] = binp.name
+    return out
+
+
+def run_reference_cutlass_single_cta(wl):
+    """The reference's own benchmark binary (oracle/_ref, built from
+    cutlass_gemm_mainloop/cutlass_gemm_bench.cu) on this box, same config."""
+    import subprocess
+    cfg = SINGLE_CTA_CFG.get(wl["dtype"])
+    if cfg is None:
+        return None
+    binp = ROOT / "oracle" / "_ref" / ("cutlass_bench_%d_%d_%d_s%d_d%d" % cfg)
+    if not binp.exists():
+        return {"unavailable": f"{binp.name} not built (oracle/ref_build.sh needs the reference tree)"}
+    try:
+        r = subprocess.run([str(binp)], capture_output=True, text=True, timeout=120)
+    except Exception as e:  # no GPU on this host, etc.
+        return {"unavailable": repr(e)[:200]}
+    if r.returncode != 0:
+        return {"unavailable": (r.stderr or r.stdout).strip()[-200:]}
+    out = parse_csv_line(r.stdout)
+    out["binary"] = binp.name
+    out["reference_published_tflops"] = REF_SINGLE_CTA_TFLOPS[wl["dtype"]]
+    return out
 
 
 def main():

@@ -34,6 +34,7 @@
 
 #include "gemm_sm100a.h"
 #include "sm100_ptx.cuh"
+#include "device_guard.cuh"
 
 using namespace sm100;
 
@@ -694,6 +695,8 @@ extern "C" int gemm_sm100a_query(const GemmArgs* args, GemmInfo* info) {
 }
 
 extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
+  StreamDeviceGuard guard(reinterpret_cast<cudaStream_t>(stream));
+  if (!guard.ok) return GEMM_ERR_LAUNCH;
   Resolved r;
   int rc = resolve(args, r);
   if (rc != GEMM_OK) return rc;
@@ -762,6 +765,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
 }
 
 extern "C" int gemm_sm100a_read_status(const int32_t* status, void* stream, int32_t* detail) {
+  StreamDeviceGuard guard(reinterpret_cast<cudaStream_t>(stream));
   if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) {
     cudaGetLastError();
     return GEMM_ERR_LAUNCH;

@@ -15,6 +15,7 @@
 #include <cstdint>
 
 #include "gemm_sm100a.h"
+#include "device_guard.cuh"
 
 namespace {
 
@@ -205,6 +206,8 @@ extern "C" int gemm_sm100a_generate(void* out, int32_t out_dtype, int32_t dist, 
   if (!out || rows < 0 || cols < 0 || ld < cols) return GEMM_ERR_BAD_ARGS;
   if (out_dtype != GEMM_DTYPE_BF16 && out_dtype != GEMM_DTYPE_FP8_E4M3) return GEMM_ERR_BAD_ARGS;
   if (rows == 0 || cols == 0) return GEMM_OK;
+  StreamDeviceGuard guard(reinterpret_cast<cudaStream_t>(cuda_stream));
+  if (!guard.ok) return GEMM_ERR_LAUNCH;
   generate_kernel<<<grid_for(rows * cols), 256, 0, reinterpret_cast<cudaStream_t>(cuda_stream)>>>(
       out, out_dtype, dist, scale, stream_key(seed, stream_id), row0, rows, cols, ld);
   if (cudaGetLastError() != cudaSuccess) return GEMM_ERR_LAUNCH;
@@ -218,6 +221,8 @@ extern "C" int gemm_sm100a_generate_nvfp4(void* out_packed, void* out_scales, fl
   if (!out_packed || !out_scales || rows < 0 || cols % 64 != 0 || rows % 128 != 0 || row0 % 128 != 0)
     return GEMM_ERR_BAD_ARGS;
   if (rows == 0 || cols == 0) return GEMM_OK;
+  StreamDeviceGuard guard(reinterpret_cast<cudaStream_t>(cuda_stream));
+  if (!guard.ok) return GEMM_ERR_LAUNCH;
   generate_nvfp4_kernel<<<grid_for(rows * (cols / 16)), 256, 0, reinterpret_cast<cudaStream_t>(cuda_stream)>>>(
       reinterpret_cast<uint8_t*>(out_packed), reinterpret_cast<uint8_t*>(out_scales), scale,
       stream_key(seed, stream_id), row0, rows, cols);
