@@ -38,6 +38,33 @@
 
 using namespace sm100;
 
+// Tuning switches (compile time).
+#ifndef GEMM_L2_PROMOTION
+#define GEMM_L2_PROMOTION CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+#endif
+#ifndef GEMM_TMA_CACHE_HINT
+#define GEMM_TMA_CACHE_HINT 1   // 1: loads carry an L2 evict_normal policy; 0: no hint
+#endif
+#ifndef GEMM_TRACE
+#define GEMM_TRACE 0            // 1: log CTA 0's pipeline events (trace builds only)
+#endif
+
+#if GEMM_TRACE
+// Pipeline event log of CTA 0 (trace builds only).  Each role writes its own
+// region with plain stores (no atomics on the critical path); entry =
+// clock64 << 16 | role << 12 | kind << 8 | stage.
+constexpr unsigned kTraceRegion = 1u << 14;
+__device__ unsigned long long g_trace_log[4 * kTraceRegion];
+#define TRACE_EVENT(role, kind, stage)                                                     \
+  do {                                                                                     \
+    if (blockIdx.x == 0 && trace_i < kTraceRegion)                                         \
+      g_trace_log[(role) * kTraceRegion + trace_i++] =                                     \
+          ((unsigned long long)clock64() << 16) | ((role) << 12) | ((kind) << 8) | ((stage) & 0xFF); \
+  } while (0)
+#else
+#define TRACE_EVENT(role, kind, stage) do { } while (0)
+#endif
+
 namespace {
 
 // Threads per CTA: producer warp + MMA warp + EPI_WARPS epilogue warps.
@@ -128,7 +155,7 @@ constexpr uint32_t kWaitHintNs = 200000;
 template <bool kCluster>
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const SharedCtl& c,
                                          uint32_t role, uint32_t idx) {
-  if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  if (kCluster ? mbar_test_wait_cluster(bar, parity) : mbar_test_wait(bar, parity)) return true;
   uint64_t t0 = 0;
   for (uint32_t probe = 1;; ++probe) {
     if (kCluster ? mbar_try_wait_cluster_hint(bar, parity, kWaitHintNs) : mbar_try_wait_hint(bar, parity, kWaitHintNs))
@@ -257,6 +284,8 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // ------------------------------------------------------------ producer
     if (lane == 0 && !(p.flags & GEMM_FLAG_INJECT_STALL)) {
       const uint64_t policy = policy_evict_normal();
+      unsigned trace_i = 0;
+      (void)trace_i;
       const uint32_t leader_full = CG == 2 ? mapa_shared(full_bar, 0) : full_bar;
       const uint32_t tx_bytes = p.stage_bytes * CG;
       int stage = 0;
@@ -297,6 +326,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const int32_t n0 = un * BN + (int32_t)cta_rank * B_BOX;
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!wait_bar<false>(empty_bar + 8u * stage, phase ^ 1u, ctl, ROLE_PRODUCER, stage)) { ok = false; break; }
+          TRACE_EVENT(1u, 1u, stage);
           if (p.l2_prefetch > 0) pf_step();
           const uint32_t sbase = ring + (uint32_t)stage * p.stage_bytes;
           const uint32_t fb = full_bar + 8u * stage;
@@ -334,6 +364,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
               bulk_load(sf_base + (uint32_t)nsf * 512u * (1 + bb), sfb_src, (uint32_t)nsf * 512u, target, policy);
             }
           }
+          TRACE_EVENT(1u, 2u, stage);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == p.stages) { stage = 0; phase ^= 1u; }
@@ -351,27 +382,35 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
+      unsigned trace_i = 0;
+      (void)trace_i;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued = false;
-      for (int u = pair; u < p.num_units && ok; u += num_pairs) {
+      // Loop-invariant parameters in registers.
+      const int n_units = p.num_units, n_kb = p.num_k_blocks, n_stages = p.stages, n_atoms = p.atoms;
+      const uint32_t st_bytes = p.stage_bytes, a_bytes = p.a_atom_bytes, b_bytes = p.b_atom_bytes;
+      const uint32_t idesc = p.idesc;
+      const int n_acc = p.num_acc;
+      for (int u = pair; u < n_units && ok; u += num_pairs) {
         if (!wait_bar<CG == 2>(tempty_bar + 8u * acc, acc_phase ^ 1u, ctl, ROLE_MMA, 0x80u | acc)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        for (int kb = 0; kb < n_kb; ++kb) {
           if (!wait_bar<CG == 2>(full_bar + 8u * stage, phase, ctl, ROLE_MMA, stage)) { ok = false; break; }
+          TRACE_EVENT(2u, 1u, stage);
           tc_fence_after();
-          const uint32_t sbase = ring + (uint32_t)stage * p.stage_bytes;
-          const uint32_t bbase = sbase + (uint32_t)p.atoms * p.a_atom_bytes;
+          const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
+          const uint32_t bbase = sbase + (uint32_t)n_atoms * a_bytes;
           if constexpr (DT == 2) {
             // Copy this stage's scale factors into TMEM (columns after the
             // two accumulators), then issue the block-scaled MMAs.
-            const uint32_t sf_base = bbase + (uint32_t)p.atoms * p.b_atom_bytes;
-            const int nsf = p.atoms * 4;
-            const uint32_t sfa_t = tmem_base + (uint32_t)(p.num_acc * BN);
+            const uint32_t sf_base = bbase + (uint32_t)n_atoms * b_bytes;
+            const int nsf = n_atoms * 4;
+            const uint32_t sfa_t = tmem_base + (uint32_t)(n_acc * BN);
             const uint32_t sfb_t = sfa_t + (uint32_t)nsf * SF_COLS_A;
             for (int q = 0; q < nsf; ++q) {
               tmem_cp_32x128b_warpx4<CG>(sfa_t + (uint32_t)q * SF_COLS_A, plain_desc(sf_base + (uint32_t)q * 512u));
@@ -379,36 +418,37 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 tmem_cp_32x128b_warpx4<CG>(sfb_t + (uint32_t)q * SF_COLS_B + 4u * bb,
                                            plain_desc(sf_base + (uint32_t)nsf * 512u * (1 + bb) + (uint32_t)q * 512u));
             }
-            for (int ka = 0; ka < p.atoms; ++ka) {
-              const uint64_t ad = sw128_kmajor_desc(sbase + (uint32_t)ka * p.a_atom_bytes);
-              const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * p.b_atom_bytes);
+            for (int ka = 0; ka < n_atoms; ++ka) {
+              const uint64_t ad = sw128_kmajor_desc(sbase + (uint32_t)ka * a_bytes);
+              const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * b_bytes);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
                 const int q = ka * 4 + kk;
-                mma_nvf4<CG>(d_tmem, ad + 2u * kk, bd + 2u * kk, p.idesc,
+                mma_nvf4<CG>(d_tmem, ad + 2u * kk, bd + 2u * kk, idesc,
                              sfa_t + (uint32_t)q * SF_COLS_A, sfb_t + (uint32_t)q * SF_COLS_B,
                              (kb | ka | kk) != 0);
               }
             }
           } else {
-            for (int ka = 0; ka < p.atoms; ++ka) {
-              const uint64_t ad = sw128_kmajor_desc(sbase + (uint32_t)ka * p.a_atom_bytes);
-              const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * p.b_atom_bytes);
+            for (int ka = 0; ka < n_atoms; ++ka) {
+              const uint64_t ad = sw128_kmajor_desc(sbase + (uint32_t)ka * a_bytes);
+              const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * b_bytes);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
                 for (int h = 0; h < N_SUB; ++h)
                   mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
-                                   bd + (uint64_t)((h * B_BOX * 128) >> 4) + 2u * kk, p.idesc, (kb | ka | kk) != 0);
+                                   bd + (uint64_t)((h * B_BOX * 128) >> 4) + 2u * kk, idesc, (kb | ka | kk) != 0);
             }
           }
-          issued = true;
           if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3); else mma_commit(empty_bar + 8u * stage);
-          if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+          TRACE_EVENT(2u, 2u, stage);
+          issued = true;
+          if (++stage == n_stages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
         if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3); else mma_commit(tfull_bar + 8u * acc);
-        if (++acc == p.num_acc) { acc = 0; acc_phase ^= 1u; }
+        if (++acc == n_acc) { acc = 0; acc_phase ^= 1u; }
       }
       if (!ok && issued) {
         // Wait (bounded) until every MMA already issued has finished with TMEM.
@@ -630,7 +670,7 @@ bool encode_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType t, uint64_t 
   cuuint32_t estr[2] = {1, 1};
   CUresult res = g_encode(m, t, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                          GEMM_L2_PROMOTION, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return res == CUDA_SUCCESS;
 }
 
@@ -709,7 +749,8 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   const int64_t eb_num = r.dt == 0 ? 2 : 1, eb_den = r.dt == 2 ? 2 : 1;   // bytes per element = num/den
   const uint64_t inner_k = (uint64_t)(r.dt == 2 ? a.k / 2 : a.k);       // tensor-map elements along K
   const uint32_t box_inner = bf ? 64u : 128u;
-  if (!encode_2d(&tma_a, a.a, t, inner_k, (uint64_t)a.m, (uint64_t)(a.lda * eb_num / eb_den), box_inner, 128u))
+  if (!encode_2d(&tma_a, a.a, t, inner_k, (uint64_t)a.m, (uint64_t)(a.lda * eb_num / eb_den), box_inner,
+                 128u))
     return GEMM_ERR_CANNOT_IMPLEMENT;
   if (!encode_2d(&tmb_b, a.b, t, inner_k, (uint64_t)a.n, (uint64_t)(a.ldb * eb_num / eb_den), box_inner,
                  (uint32_t)((r.bn > 256 ? 256 : r.bn) / r.cg)))
@@ -792,3 +833,15 @@ extern "C" const char* gemm_sm100a_strerror(int code) {
 }
 
 extern "C" int gemm_sm100a_version(void) { return 100; }
+
+#if GEMM_TRACE
+// Trace builds only: copy CTA 0's event log (4 regions of 16384 entries, one
+// per role) to `out` and clear it.  Returns the number of entries copied.
+extern "C" int gemm_sm100a_trace_read(unsigned long long* out, int max) {
+  const int n = max < (int)(4 * kTraceRegion) ? max : (int)(4 * kTraceRegion);
+  if (cudaMemcpyFromSymbol(out, g_trace_log, (size_t)n * sizeof(unsigned long long)) != cudaSuccess) return -1;
+  static unsigned long long zeros[4 * kTraceRegion];
+  cudaMemcpyToSymbol(g_trace_log, zeros, sizeof(zeros));
+  return n;
+}
+#endif
