@@ -289,7 +289,9 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     dt = dtype_code(pkg, wl["dtype"])
     m, n, k = wl["m"], wl["n"], wl["k"]
     knobs = effective_knobs(wl, args)
-    n0 = rank * n
+    from microbench_blackwell_b200 import nsplit
+    slab = nsplit.partition(n * world, world, rank, align=knobs.get("tile_n", 256))
+    n0 = slab.n0
     with torch.cuda.stream(stream):
         ops = pkg.make_operands(dt, m, n, k, seed=args.seed,
                                 a_dist=dist_code(pkg, wl["a"][0]), a_scale=wl["a"][1],
@@ -335,10 +337,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize(dev)
     barrier()
     ms = start.elapsed_time(end)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = nsplit.max_over_ranks(ms, device=dev)
     rc, detail = pkg.read_status(status.data_ptr(), st)
     if rc != 0:
         raise SystemExit(f"device status error 0x{detail & 0xffffffff:08x}")
@@ -347,6 +346,24 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     value = flop * world / (ms_per_step * 1e-3) / 1e12
     achieved = flop / (ms / args.steps * 1e-3) / 1e12          # this rank's kernel, per launch
     clocks = sampler.summary()
+
+    # ---------------------------------------------------------- optional all-gather of D (N > 1)
+    allgather = None
+    if world > 1:
+        with torch.cuda.stream(stream):
+            nsplit.gather_columns(ops.d, n * world)                 # warm-up
+            stream.synchronize()
+            barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            full = nsplit.gather_columns(ops.d, n * world)
+            g1.record(stream)
+        g1.synchronize()
+        ag_ms = nsplit.max_over_ranks(g0.elapsed_time(g1), device=dev)
+        recv = (world - 1) * ops.d.numel() * ops.d.element_size()
+        allgather = {"ms": ag_ms, "bytes_received_per_rank": recv,
+                     "GBps_per_rank": recv / (ag_ms * 1e-3) / 1e9, "collective": "ncclAllGather (torch.distributed)"}
+        del full
 
     # ---------------------------------------------------------- end to end (host buffers)
     e2e = run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank)
@@ -384,6 +401,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
         "gpu_launches": args.steps,
         "cpu_baseline": cpu,
         "single_cta": single,
+        "allgather": allgather,
         "kernel": {"grid": info.grid_ctas, "stages": info.stages, "tile": [info.tile_m, info.tile_n, info.tile_k],
                    "smem_bytes": info.smem_bytes, "tmem_columns": info.tmem_columns},
     }
