@@ -604,6 +604,7 @@ int resolve(const GemmArgs* a, Resolved& r) {
     if (r.cg != 1) FAIL("NVFP4 is implemented for cta_group 1 only");
     if (a->k % r.tile_k != 0) FAIL("NVFP4 needs k %% tile_k == 0");
     if (a->m % 128 != 0 || a->n % r.bn != 0) FAIL("NVFP4 needs m %% 128 == 0 and n %% tile_n == 0");
+    if (r.bn % 128 != 0) FAIL("NVFP4 needs tile_n 128 or 256 (scale atoms are 128 rows)");
     if (((uintptr_t)a->sfa | (uintptr_t)a->sfb) & 15) FAIL("sfa/sfb must be 16-byte aligned");
   }
 

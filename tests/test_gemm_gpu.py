@@ -226,3 +226,70 @@ def test_config3_fp8_16384_pair_sampled(pkg, orc, cuda):
     got = orc.bf16_bits_to_f32(D[np.ix_(cols, rows)].T)
     err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
     assert err <= TOL[1], err
+
+
+# --------------------------------------------------------------------------- NVFP4 (1-SM)
+E2M1_ONE = 0x2          # e2m1 code of 1.0
+UE4M3_ONE = 0x38        # e4m3 code of 1.0
+
+
+def nvfp4_identity(torch_dev, n, k):
+    """Packed e2m1 identity rows (B[n][k] = 1 if n == k) with all scales 1.0."""
+    packed = torch.zeros((n, k // 2), dtype=torch.uint8)
+    for i in range(min(n, k)):
+        packed[i, i // 2] = E2M1_ONE << (4 * (i % 2))
+    return packed.to(torch_dev)
+
+
+@pytest.mark.parametrize("tile_n", [128, 256])
+def test_nvfp4_identity_b_reproduces_a_with_its_block_scales(pkg, orc, cuda, tile_n):
+    """D = A . I^T reproduces A's dequantised values (e2m1 x its per-16 ue4m3 scale), exactly:
+    pins the packed-fp4 smem descriptors and the SFA scale layout in TMEM."""
+    m, n, k = 256, 256, 512
+    ops = pkg.make_operands(pkg.NVFP4, m, n, k, seed=2, device=cuda)
+    ops.b.copy_(nvfp4_identity(cuda, n, k))
+    ops.sfb.fill_(UE4M3_ONE)
+    pkg.gemm(ops, tile_n=tile_n, tile_k=256)
+    A = orc.dequant_nvfp4(ops.a.cpu().numpy(), ops.sfa.cpu().numpy(), k)
+    D = orc.bf16_bits_to_f32(raw_u16(ops.d.t().contiguous()))
+    np.testing.assert_array_equal(D, A[:, :n])
+
+
+def test_nvfp4_identity_a_reproduces_b_with_its_block_scales(pkg, orc, cuda):
+    """The mirror case pins the SFB layout (256 B rows = two 128-row scale atoms)."""
+    m, n, k = 256, 256, 512
+    ops = pkg.make_operands(pkg.NVFP4, m, n, k, seed=3, device=cuda)
+    ops.a.copy_(nvfp4_identity(cuda, m, k))
+    ops.sfa.fill_(UE4M3_ONE)
+    pkg.gemm(ops, tile_n=256, tile_k=256)
+    B = orc.dequant_nvfp4(ops.b.cpu().numpy(), ops.sfb.cpu().numpy(), k)
+    D = orc.bf16_bits_to_f32(raw_u16(ops.d.t().contiguous()))
+    np.testing.assert_array_equal(D, B[:, :m].T)
+
+
+@pytest.mark.parametrize("m,n,k,tile_n,stages", [(256, 256, 1024, 256, 0), (384, 512, 2048, 128, 0),
+                                                 (128, 256, 256, 256, 2), (512, 768, 4096, 256, 3)])
+def test_nvfp4_matches_oracle(pkg, orc, cuda, m, n, k, tile_n, stages):
+    ops = pkg.make_operands(pkg.NVFP4, m, n, k, seed=0, device=cuda)
+    pkg.gemm(ops, tile_n=tile_n, tile_k=256, stages=stages)
+    err = rel_err(orc, pkg, ops)
+    assert err <= TOL[2], err
+
+
+def test_config4_nvfp4_mlp_sampled(pkg, orc, cuda):
+    """NVFP4 M=8192, N=28672, K=8192; sampled fp64 check."""
+    m, n, k = 8192, 28672, 8192
+    ops = pkg.make_operands(pkg.NVFP4, m, n, k, seed=0, device=cuda)
+    pkg.gemm(ops, tile_n=256, tile_k=256)
+    rng = np.random.default_rng(4)
+    rows = np.sort(rng.choice(m // 128, 1, replace=False))[0] * 128 + np.arange(128)   # one 128-row scale block
+    cols = np.sort(rng.choice(n, 96, replace=False))
+    A = orc.dequant_nvfp4(ops.a[rows[0]:rows[0] + 128].cpu().numpy(),
+                          ops.sfa[(rows[0] // 128) * (k // 64) * 512:(rows[0] // 128 + 1) * (k // 64) * 512].cpu().numpy(), k)
+    Bfull_packed = ops.b.cpu().numpy(); Bsf = ops.sfb.cpu().numpy()
+    B = orc.dequant_nvfp4(Bfull_packed, Bsf, k)[cols]
+    ref = orc.gemm_f64(A, B)
+    D = raw_u16(ops.d).reshape(n, m)
+    got = orc.bf16_bits_to_f32(D[np.ix_(cols, rows)].T)
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert err <= TOL[2], err
