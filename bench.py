@@ -32,8 +32,9 @@ ROOT = Path(__file__).resolve().parent
 PKG_DIR = ROOT / "microbench-blackwell_b200"
 
 # Reference figures used in derived keys (cited, not measured here).
-REF_UMMA_FLOP_PER_CLK_SM = {  # umma_throughput/tput_results_max.csv:13,49 (1SM M128 N256 SS)
-    "bf16": 8152.85, "e4m3": 16344.5, "nvfp4": 32721.7}
+REF_UMMA_FLOP_PER_CLK_SM = {  # umma_throughput/tput_results_max.csv:13,49,175 (1SM M128 N256 SS; nvfp4 = MXF4 row)
+    "bf16": 8152.85, "e4m3": 16344.5, "nvfp4": 32721.3}
+DENSE_RATE_VS_BF16 = {"bf16": 1.0, "e4m3": 2.0, "nvfp4": 4.0}     # tcgen05 dense rates per SM per clock
 REF_SINGLE_CTA_TFLOPS = {"bf16": 10.4596, "e4m3": 20.6377}  # cutlass_gemm_mainloop/results.csv:461,938
 
 WORKLOADS = {
@@ -51,7 +52,7 @@ WORKLOADS = {
                       knobs=dict(tile_n=256, tile_k=256, stages=0, cta_group=1, raster_group=1),
                       a=("normal", 1.0), b=("normal", 1.0), config=4),
     "e4m3_nsplit": dict(dtype="e4m3", m=16384, n=57344, k=8192,
-                        knobs=dict(tile_n=256, tile_k=128, stages=0, cta_group=2),
+                        knobs=dict(tile_n=512, tile_k=128, stages=0, cta_group=2, raster_group=16),
                         a=("normal", 0.25), b=("normal", 0.02), config=5),
     "bf16_256": dict(dtype="bf16", m=256, n=256, k=256,
                      knobs=dict(tile_n=256, tile_k=64, stages=4, cta_group=1),
@@ -368,6 +369,13 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     # ---------------------------------------------------------- end to end (host buffers)
     e2e = run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank)
 
+    # ---------------------------------------------------------- the other dtypes
+    per_dtype = None
+    if not args.no_per_dtype:
+        del ops
+        torch.cuda.empty_cache()
+        per_dtype = run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, clocks.get("sm_mhz"))
+
     # ---------------------------------------------------------- single-CTA mainloop (reference experiment)
     single = run_single_cta(pkg, wl, dev, stream) if (rank == 0 and wl["dtype"] in SINGLE_CTA_CFG) else None
 
@@ -379,7 +387,9 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu, _ = cpu_gemm_sample(wl, budget_s=12.0, seed=args.seed)
-    peak_key = "bf16_tflops" if wl["dtype"] == "bf16" else None
+    peak = peaks["bf16_tflops"] * DENSE_RATE_VS_BF16[wl["dtype"]]
+    peak_src = f"{peaks['source']} cuBLAS bf16 burst (MEASURED_PEAKS.json)" + (
+        "" if wl["dtype"] == "bf16" else f" x {DENSE_RATE_VS_BF16[wl['dtype']]:.0f} (dense {wl['dtype']} rate), derived")
     line = {
         "metric": "GEMM TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -387,10 +397,10 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
         "dtype": wl["dtype"], "data": "synthetic (seeded, generated on device)",
         "config": config_block(wl, world, args),
         "roofline": {"bound": "tensor", "achieved": achieved,
-                     "peak": peaks["bf16_tflops"] if peak_key else None,
+                     "peak": peak,
                      "unit": "TFLOP/s",
-                     "frac": achieved / peaks["bf16_tflops"] if peak_key else None,
-                     "peak_source": f"{peaks['source']} cuBLAS bf16 burst (MEASURED_PEAKS.json)",
+                     "frac": achieved / peak,
+                     "peak_source": peak_src,
                      "traffic": ncu_traffic(args.workload),
                      "algorithmic_bytes": m * k * elem_bytes(wl["dtype"]) + n * k * elem_bytes(wl["dtype"]) + m * n * 2},
         "sol_umma": {"pct": (100.0 * achieved / (umma * 148 * sm_mhz * 1e6 / 1e12)) if sm_mhz else None,
@@ -402,10 +412,69 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
         "cpu_baseline": cpu,
         "single_cta": single,
         "allgather": allgather,
+        "per_dtype": per_dtype,
         "kernel": {"grid": info.grid_ctas, "stages": info.stages, "tile": [info.tile_m, info.tile_n, info.tile_k],
                    "smem_bytes": info.smem_bytes, "tmem_columns": info.tmem_columns},
     }
     print(json.dumps(line), flush=True)
+
+
+PER_DTYPE = [
+    # (label, workload, scaling): weak = every rank does the full per-GPU problem on its own
+    # N slab; strong = the workload's N is split across the ranks (config 5).
+    ("e4m3_config3", "e4m3_16384_2sm", "weak"),
+    ("nvfp4_config4", "nvfp4_mlp", "weak"),
+    ("e4m3_nsplit_config5", "e4m3_nsplit", "strong"),
+]
+
+
+def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
+    """Time the other BASELINE configurations (fewer steps) for the per-dtype metric."""
+    import torch
+    import torch.distributed as dist
+    from microbench_blackwell_b200 import nsplit
+    out = {}
+    steps = max(5, min(args.steps, 20))
+    for label, name, scaling in PER_DTYPE:
+        wl = WORKLOADS[name]
+        m, k = wl["m"], wl["k"]
+        if scaling == "strong":
+            slab = nsplit.partition(wl["n"], world, rank, align=wl["knobs"]["tile_n"])
+        else:
+            slab = nsplit.partition(wl["n"] * world, world, rank, align=wl["knobs"]["tile_n"])
+        n = slab.n_local
+        dt = dtype_code(pkg, wl["dtype"])
+        ops = pkg.make_operands(dt, m, n, k, seed=args.seed, a_dist=dist_code(pkg, wl["a"][0]), a_scale=wl["a"][1],
+                                b_dist=dist_code(pkg, wl["b"][0]), b_scale=wl["b"][1], n0=slab.n0,
+                                device=dev, stream=stream.cuda_stream)
+        g = pkg.make_args(dtype=dt, m=m, n=n, k=k, a=ops.a.data_ptr(), b=ops.b.data_ptr(), d=ops.d.data_ptr(),
+                          sfa=None if ops.sfa is None else ops.sfa.data_ptr(),
+                          sfb=None if ops.sfb is None else ops.sfb.data_ptr(), **wl["knobs"])
+        L = pkg.lib()
+        sp = C.c_void_p(stream.cuda_stream)
+        for _ in range(3):
+            L.gemm_sm100a_launch(C.byref(g), sp)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(steps):
+            L.gemm_sm100a_launch(C.byref(g), sp)
+        s1.record(stream)
+        s1.synchronize()
+        ms = nsplit.max_over_ranks(s0.elapsed_time(s1) / steps, device=dev)
+        flop_total = pkg.flops(m, n, k) * world
+        tf = flop_total / (ms * 1e-3) / 1e12
+        per_gpu = tf / world
+        umma = REF_UMMA_FLOP_PER_CLK_SM[wl["dtype"]]
+        out[label] = {"workload": name, "baseline_config": wl["config"], "scaling": scaling,
+                      "m": m, "n_total": n * world, "k": k, "knobs": wl["knobs"], "steps": steps,
+                      "ms_per_step": ms, "tflops": tf, "tflops_per_gpu": per_gpu,
+                      "pct_umma_peak": (100.0 * per_gpu / (umma * 148 * sm_mhz * 1e6 / 1e12)) if sm_mhz else None}
+        del ops
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank):
@@ -520,6 +589,7 @@ def main():
     ap.add_argument("--raster-group", type=int, default=None)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-dtype", action="store_true", help="skip the other BASELINE configurations")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
