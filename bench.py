@@ -383,7 +383,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
         return
     peaks = measured_peaks()
     sm_mhz = clocks.get("sm_mhz")
-    umma = REF_UMMA_FLOP_PER_CLK_SM[wl["dtype"]]
+    umma_peak = measured_umma_peak(pkg, wl["dtype"], dev)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu, _ = cpu_gemm_sample(wl, budget_s=12.0, seed=args.seed)
@@ -403,9 +403,12 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
                      "peak_source": peak_src,
                      "traffic": ncu_traffic(args.workload),
                      "algorithmic_bytes": m * k * elem_bytes(wl["dtype"]) + n * k * elem_bytes(wl["dtype"]) + m * n * 2},
-        "sol_umma": {"pct": (100.0 * achieved / (umma * 148 * sm_mhz * 1e6 / 1e12)) if sm_mhz else None,
-                     "flop_per_clk_per_sm": umma, "sm_mhz": sm_mhz,
-                     "source": "reference umma_throughput/tput_results_max.csv (1SM M128 N256 SS)"},
+        "sol_umma": {"pct_measured_umma_peak": 100.0 * achieved / umma_peak["tflops"],
+                     "umma_peak_tflops": umma_peak["tflops"], "umma_flop_per_clk_per_sm": umma_peak["flop_per_clk_per_sm"],
+                     "umma_sm_mhz": umma_peak["sm_mhz"], "source": umma_peak["source"],
+                     "reference_flop_per_clk_per_sm": REF_UMMA_FLOP_PER_CLK_SM[wl["dtype"]],
+                     "pct_at_gemm_clock": (100.0 * achieved / (umma_peak["flop_per_clk_per_sm"] * 148 * sm_mhz * 1e6 / 1e12))
+                     if sm_mhz else None},
         "clocks": clocks,
         "e2e": e2e,
         "gpu_launches": args.steps,
@@ -426,6 +429,17 @@ PER_DTYPE = [
     ("nvfp4_config4", "nvfp4_mlp", "weak"),
     ("e4m3_nsplit_config5", "e4m3_nsplit", "strong"),
 ]
+
+
+def measured_umma_peak(pkg, dtype_name: str, dev) -> dict:
+    """Whole-GPU tcgen05 dense peak of this GPU for one dtype (CTA pairs on every SM,
+    non-zero operands), from the library's probe -- the SOL denominator."""
+    import torch
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    r = pkg.umma_peak(dtype_code(pkg, dtype_name), cta_group=2, num_ctas=sms - sms % 2, depth=256, iters=1500,
+                      device=dev)
+    r["source"] = "gemm_sm100a_umma_peak, whole GPU, M256 N256 pairs, non-zero operands"
+    return r
 
 
 def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
@@ -467,11 +481,12 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
         flop_total = pkg.flops(m, n, k) * world
         tf = flop_total / (ms * 1e-3) / 1e12
         per_gpu = tf / world
-        umma = REF_UMMA_FLOP_PER_CLK_SM[wl["dtype"]]
+        peak = measured_umma_peak(pkg, wl["dtype"], dev)
         out[label] = {"workload": name, "baseline_config": wl["config"], "scaling": scaling,
                       "m": m, "n_total": n * world, "k": k, "knobs": wl["knobs"], "steps": steps,
                       "ms_per_step": ms, "tflops": tf, "tflops_per_gpu": per_gpu,
-                      "pct_umma_peak": (100.0 * per_gpu / (umma * 148 * sm_mhz * 1e6 / 1e12)) if sm_mhz else None}
+                      "umma_peak_tflops": peak["tflops"], "umma_peak_sm_mhz": peak["sm_mhz"],
+                      "pct_measured_umma_peak": 100.0 * per_gpu / peak["tflops"]}
         del ops
         torch.cuda.empty_cache()
     return out

@@ -177,6 +177,19 @@ int gemm_sm100a_generate_nvfp4(void* out_packed, void* out_scales, float scale,
                                int64_t row0, int64_t rows, int64_t cols,
                                void* cuda_stream);
 
+/*
+ * Measured tcgen05 dense peak (replaces the reference's umma_throughput/umma_tput.cu
+ * probe, kernel :286-544, with an NVFP4 kind and a whole-GPU mode added).
+ * Launches `num_ctas` CTAs (a multiple of cta_group; one per SM at most), each
+ * issuing `iters` groups of `depth` back-to-back M=128*cta_group, N=256 MMAs of
+ * `dtype` from shared memory, one commit per group.  results (device, caller-owned,
+ * 3*num_ctas uint64) receives per CTA {clock64 cycles, %globaltimer ns, status}
+ * (zeros for the non-issuing CTA of a pair).  Returns GEMM_OK, GEMM_ERR_BAD_ARGS
+ * or GEMM_ERR_LAUNCH; asynchronous on `stream`.
+ */
+int gemm_sm100a_umma_peak(int32_t dtype, int32_t cta_group, int32_t num_ctas, int32_t depth,
+                          int32_t iters, unsigned long long* results, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

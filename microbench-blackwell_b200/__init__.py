@@ -63,7 +63,7 @@ class GemmInfo(C.Structure):
 EXPORTED = (
     "gemm_sm100a_query", "gemm_sm100a_launch", "gemm_sm100a_read_status",
     "gemm_sm100a_strerror", "gemm_sm100a_version",
-    "gemm_sm100a_generate", "gemm_sm100a_generate_nvfp4",
+    "gemm_sm100a_generate", "gemm_sm100a_generate_nvfp4", "gemm_sm100a_umma_peak",
 )
 
 
@@ -99,6 +99,8 @@ def lib():
         L.gemm_sm100a_generate.argtypes = [vp, i32, i32, f32, u64, u64, i64, i64, i64, i64, vp]
         L.gemm_sm100a_generate_nvfp4.restype = C.c_int
         L.gemm_sm100a_generate_nvfp4.argtypes = [vp, vp, f32, u64, u64, i64, i64, i64, vp]
+        L.gemm_sm100a_umma_peak.restype = C.c_int
+        L.gemm_sm100a_umma_peak.argtypes = [i32, i32, i32, i32, i32, vp, vp]
         _lib = L
     return _lib
 
@@ -169,6 +171,40 @@ def generate_nvfp4(packed_ptr: int, scales_ptr: int, scale: float, seed: int, st
                                           stream_id, row0, rows, cols, C.c_void_p(cuda_stream))
     if rc != OK:
         raise GemmError(rc, "gemm_sm100a_generate_nvfp4")
+
+
+K_ELEMS_PER_MMA = {BF16: 16, FP8_E4M3: 32, NVFP4: 64}
+
+
+def umma_peak(dtype: int, cta_group: int = 1, num_ctas: int = 1, depth: int = 256, iters: int = 200,
+              device=None) -> dict:
+    """Run the tcgen05 peak probe and summarise it.
+
+    flop_per_clk_per_sm: median over issuing CTAs of FLOPs / clock64 cycles, per SM
+    (a CTA pair counts as two SMs); sm_mhz: median cycles / ns; tflops: total FLOPs of
+    all issuing CTAs / the longest CTA time (the whole-GPU dense peak when num_ctas
+    covers every SM)."""
+    import statistics
+    import torch
+    dev = torch.device("cuda" if device is None else device)
+    res = torch.zeros(3 * num_ctas, dtype=torch.int64, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib().gemm_sm100a_umma_peak(dtype, cta_group, num_ctas, depth, iters, C.c_void_p(res.data_ptr()),
+                                     C.c_void_p(st))
+    if rc != OK:
+        raise GemmError(rc, "gemm_sm100a_umma_peak")
+    torch.cuda.synchronize(dev)
+    r = res.view(num_ctas, 3).cpu().tolist()
+    leaders = [x for x in r if x[0] > 0]
+    if any(x[2] for x in r):
+        raise GemmError(ERR_TIMEOUT, "umma_peak wait")
+    flop_per_mma = 2.0 * 128 * cta_group * 256 * K_ELEMS_PER_MMA[dtype]
+    total = flop_per_mma * depth * iters
+    fpc = [total / x[0] / cta_group for x in leaders]
+    mhz = [x[0] / x[1] * 1e3 for x in leaders]
+    return {"dtype": DTYPE_NAMES[dtype], "cta_group": cta_group, "num_ctas": num_ctas, "depth": depth,
+            "iters": iters, "flop_per_clk_per_sm": statistics.median(fpc), "sm_mhz": statistics.median(mhz),
+            "tflops": total * len(leaders) / (max(x[1] for x in leaders) * 1e-9) / 1e12}
 
 
 def sf_bytes(rows: int, cols: int) -> int:
