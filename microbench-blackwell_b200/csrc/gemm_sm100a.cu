@@ -11,7 +11,8 @@
 //
 // One CTA of 192 threads per SM (persistent over output tiles):
 //   warp 0      TMA producer: 128B-swizzled A/B k-atoms into a STAGES-deep
-//               shared-memory ring, guarded by full/empty mbarriers.
+//               shared-memory ring, guarded by full/empty mbarriers (a TILE_K
+//               narrower than 128 bytes is one 64B- or 32B-swizzled atom).
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer; commits
 //               free ring slots and hands finished accumulators to the epilogue.
 //   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (32 lanes each),
@@ -88,6 +89,7 @@ struct KernelParams {
   int32_t tmem_cols;
   uint32_t stage_bytes;   // per CTA: A + B (+ scale factors)
   uint32_t a_atom_bytes, b_atom_bytes;
+  uint32_t row_bytes;     // bytes of one operand row in a K atom: 128, 64 or 32 (the swizzle width)
   uint32_t sf_stage_bytes;  // NVFP4: SFA + SFB bytes per stage per CTA
   uint32_t idesc;
   float alpha;
@@ -223,7 +225,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   constexpr int EPI_WARPS = epi_warps_for(BN);
   constexpr int MMA_M = BM * CG;
   constexpr int KIND = DT == 0 ? 0 : 1;
-  constexpr int MAP_ELEMS_PER_ATOM = DT == 0 ? 64 : 128;  // tensor-map elements per 128 B
+  const int MAP_ELEMS_PER_ATOM = (int)p.row_bytes / (DT == 0 ? 2 : 1);  // tensor-map elements per atom row
   constexpr int SF_COLS_A = 4;            // TMEM columns of SFA per 64-element K step (NVFP4)
   constexpr int SF_COLS_B = ((BN + 127) / 128) * 4;
 
@@ -340,12 +342,12 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
               tma_load_2d_pair(a_dst, &tmap_a, target, x, m0, policy);
 #pragma unroll
               for (int h = 0; h < N_SUB; ++h)
-                tma_load_2d_pair(b_dst + (uint32_t)(h * B_BOX * 128), &tmap_b, target, x, n0 + h * MMA_N, policy);
+                tma_load_2d_pair(b_dst + (uint32_t)(h * B_BOX) * p.row_bytes, &tmap_b, target, x, n0 + h * MMA_N, policy);
             } else {
               tma_load_2d(a_dst, &tmap_a, target, x, m0, policy);
 #pragma unroll
               for (int h = 0; h < N_SUB; ++h)
-                tma_load_2d(b_dst + (uint32_t)(h * B_BOX * 128), &tmap_b, target, x, n0 + h * MMA_N, policy);
+                tma_load_2d(b_dst + (uint32_t)(h * B_BOX) * p.row_bytes, &tmap_b, target, x, n0 + h * MMA_N, policy);
             }
           }
           if constexpr (DT == 2) {
@@ -394,6 +396,8 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const int n_units = p.num_units, n_kb = p.num_k_blocks, n_stages = p.stages, n_atoms = p.atoms;
       const uint32_t st_bytes = p.stage_bytes, a_bytes = p.a_atom_bytes, b_bytes = p.b_atom_bytes;
       const uint32_t idesc = p.idesc;
+      const uint32_t row_b = p.row_bytes;
+      const int k_steps = (int)(row_b / 32u);   // 32 bytes of K per MMA
       const int n_acc = p.num_acc;
       for (int u = pair; u < n_units && ok; u += num_pairs) {
         if (!wait_bar<CG == 2>(tempty_bar + 8u * acc, acc_phase ^ 1u, ctl, ROLE_MMA, 0x80u | acc)) { ok = false; break; }
@@ -419,8 +423,8 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                            plain_desc(sf_base + (uint32_t)nsf * 512u * (1 + bb) + (uint32_t)q * 512u));
             }
             for (int ka = 0; ka < n_atoms; ++ka) {
-              const uint64_t ad = sw128_kmajor_desc(sbase + (uint32_t)ka * a_bytes);
-              const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * b_bytes);
+              const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, row_b);
+              const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, row_b);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
                 const int q = ka * 4 + kk;
@@ -431,14 +435,23 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
             }
           } else {
             for (int ka = 0; ka < n_atoms; ++ka) {
-              const uint64_t ad = sw128_kmajor_desc(sbase + (uint32_t)ka * a_bytes);
-              const uint64_t bd = sw128_kmajor_desc(bbase + (uint32_t)ka * b_bytes);
+              const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, row_b);
+              const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, row_b);
+              if (k_steps == 4) {   // 128-byte rows: the fully unrolled common case
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
+                for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-                for (int h = 0; h < N_SUB; ++h)
-                  mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
-                                   bd + (uint64_t)((h * B_BOX * 128) >> 4) + 2u * kk, idesc, (kb | ka | kk) != 0);
+                  for (int h = 0; h < N_SUB; ++h)
+                    mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
+                                     bd + (uint64_t)((h * B_BOX * 128) >> 4) + 2u * kk, idesc, (kb | ka | kk) != 0);
+              } else {              // 64- or 32-byte rows (narrow TILE_K): 2 or 1 K steps
+                for (int kk = 0; kk < k_steps; ++kk)
+#pragma unroll
+                  for (int h = 0; h < N_SUB; ++h)
+                    mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
+                                     bd + (uint64_t)(((uint32_t)(h * B_BOX) * row_b) >> 4) + 2u * kk, idesc,
+                                     (kb | ka | kk) != 0);
+              }
             }
           }
           if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3); else mma_commit(empty_bar + 8u * stage);
@@ -547,6 +560,7 @@ struct Resolved {
   uint32_t a_atom_bytes, b_atom_bytes, sf_stage_bytes, stage_bytes;
   int64_t smem_bytes;
   int tmem_cols, num_acc, threads;
+  uint32_t row_bytes;
   int num_m_units, num_n_units, num_units, num_k_blocks;
   int grid, num_sms, raster_group;
   char reason[128];
@@ -589,8 +603,19 @@ int resolve(const GemmArgs* a, Resolved& r) {
   if (!supported_bn(r.cg, r.bn)) FAIL("tile_n %d unsupported for cta_group %d", r.bn, r.cg);
   const int ae = atom_elems(r.dt);
   r.tile_k = a->tile_k == 0 ? ae : a->tile_k;
-  if (r.tile_k % ae != 0) FAIL("tile_k %d must be a multiple of %d (one 128-byte swizzle atom)", r.tile_k, ae);
-  r.atoms = r.tile_k / ae;
+  // A stage narrower than one 128-byte swizzle row uses the 64- or 32-byte
+  // swizzle with one atom; wider stages are whole 128-byte atoms.
+  const int mma_k = ae / 4;   // K elements of one MMA (32 bytes)
+  if (r.tile_k < ae && r.dt != 2 && (r.tile_k == mma_k || r.tile_k == 2 * mma_k)) {
+    r.row_bytes = (uint32_t)(r.tile_k / mma_k) * 32u;
+    r.atoms = 1;
+  } else {
+    if (r.tile_k % ae != 0)
+      FAIL("tile_k %d must be a multiple of %d (one 128-byte swizzle atom)%s", r.tile_k, ae,
+           r.dt == 2 ? "" : ", or one or two MMA K steps");
+    r.row_bytes = 128u;
+    r.atoms = r.tile_k / ae;
+  }
 
   // Element size in bytes (NVFP4: half a byte) and alignment (128-bit, as the reference's Alignment{A,B,D}).
   const int64_t bits = r.dt == 0 ? 16 : (r.dt == 1 ? 8 : 4);
@@ -608,8 +633,8 @@ int resolve(const GemmArgs* a, Resolved& r) {
     if (((uintptr_t)a->sfa | (uintptr_t)a->sfb) & 15) FAIL("sfa/sfb must be 16-byte aligned");
   }
 
-  r.a_atom_bytes = 128u * 128u;
-  r.b_atom_bytes = (uint32_t)(r.bn / r.cg) * 128u;
+  r.a_atom_bytes = 128u * r.row_bytes;
+  r.b_atom_bytes = (uint32_t)(r.bn / r.cg) * r.row_bytes;
   r.sf_stage_bytes = 0;
   if (r.dt == 2) {
     const int b_blocks = (r.bn / r.cg + 127) / 128;
@@ -664,13 +689,15 @@ int resolve(const GemmArgs* a, Resolved& r) {
 #undef FAIL
 
 bool encode_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType t, uint64_t inner, uint64_t outer,
-               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, uint32_t swizzle_bytes) {
+  const CUtensorMapSwizzle swz = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                               : (swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult res = g_encode(m, t, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                           GEMM_L2_PROMOTION, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return res == CUDA_SUCCESS;
 }
@@ -749,12 +776,12 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   const CUtensorMapDataType t = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const int64_t eb_num = r.dt == 0 ? 2 : 1, eb_den = r.dt == 2 ? 2 : 1;   // bytes per element = num/den
   const uint64_t inner_k = (uint64_t)(r.dt == 2 ? a.k / 2 : a.k);       // tensor-map elements along K
-  const uint32_t box_inner = bf ? 64u : 128u;
+  const uint32_t box_inner = bf ? r.row_bytes / 2 : r.row_bytes;
   if (!encode_2d(&tma_a, a.a, t, inner_k, (uint64_t)a.m, (uint64_t)(a.lda * eb_num / eb_den), box_inner,
-                 128u))
+                 128u, r.row_bytes))
     return GEMM_ERR_CANNOT_IMPLEMENT;
   if (!encode_2d(&tmb_b, a.b, t, inner_k, (uint64_t)a.n, (uint64_t)(a.ldb * eb_num / eb_den), box_inner,
-                 (uint32_t)((r.bn > 256 ? 256 : r.bn) / r.cg)))
+                 (uint32_t)((r.bn > 256 ? 256 : r.bn) / r.cg), r.row_bytes))
     return GEMM_ERR_CANNOT_IMPLEMENT;
 
   KernelParams p;
@@ -764,6 +791,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   p.num_k_blocks = r.num_k_blocks; p.atoms = r.atoms; p.stages = r.stages;
   p.raster_group = r.raster_group; p.tmem_cols = r.tmem_cols;
   p.stage_bytes = r.stage_bytes; p.a_atom_bytes = r.a_atom_bytes; p.b_atom_bytes = r.b_atom_bytes;
+  p.row_bytes = r.row_bytes;
   p.sf_stage_bytes = r.sf_stage_bytes;
   p.idesc = make_idesc(r.dt, r.bm, r.bn > 256 ? 256 : r.bn);
   p.num_acc = r.num_acc;

@@ -317,6 +317,19 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
   return d;
 }
+// K-major operand in the 128/64/32-byte swizzle canonical layout with rows of
+// `row_bytes` (128, 64 or 32): 8-row atoms of 8*row_bytes stacked every
+// 8*row_bytes (stride byte offset), layout type 2 / 4 / 6 = SWIZZLE_128B / 64B / 32B.
+__device__ __forceinline__ uint64_t swz_kmajor_desc(uint32_t smem_addr, uint32_t row_bytes) {
+  const uint64_t layout = row_bytes == 128 ? 2 : (row_bytes == 64 ? 4 : 6);
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)((8 * row_bytes) >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= layout << 61;
+  return d;
+}
 // Descriptor of a non-swizzled contiguous block (scale-factor copies):
 // 8-row x 16-byte core matrices, stride byte offset 128 B between row groups.
 __device__ __forceinline__ uint64_t plain_desc(uint32_t smem_addr) {

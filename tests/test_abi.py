@@ -82,7 +82,8 @@ def test_pair_mode_resolution(pkg):
 
 @pytest.mark.parametrize("kw,frag", [
     (dict(tile_n=48), b"tile_n"),
-    (dict(tile_k=32), b"tile_k"),
+    (dict(tile_k=48), b"tile_k"),
+    (dict(tile_k=96), b"tile_k"),
     (dict(cta_group=3), b"cta_group"),
     (dict(lda=8191), b"lda"),
     (dict(k=4, lda=8192, ldb=8192), b"k must"),
@@ -93,6 +94,18 @@ def test_cannot_implement_reasons(pkg, kw, frag):
     rc, info = pkg.query(_args(pkg, **kw))
     assert rc in (pkg.ERR_CANNOT_IMPLEMENT, pkg.ERR_BAD_ARGS)
     assert frag in info.reason, info.reason
+
+
+@pytest.mark.parametrize("dtype,tile_k,row_bytes", [("bf16", 16, 32), ("bf16", 32, 64),
+                                                    ("fp8", 32, 32), ("fp8", 64, 64)])
+def test_narrow_tile_k_uses_narrow_swizzle(pkg, dtype, tile_k, row_bytes):
+    """TILE_K below one 128-byte row (the reference sweeps bf16 16/32 and fp8
+    32/64) is one 64- or 32-byte swizzle atom per stage."""
+    dt = pkg.BF16 if dtype == "bf16" else pkg.FP8_E4M3
+    rc, info = pkg.query(_args(pkg, dtype=dt, tile_n=256, tile_k=tile_k))
+    assert rc == pkg.OK, info.reason
+    assert info.tile_k == tile_k
+    assert info.smem_bytes_per_stage == (128 + 256) * row_bytes
 
 
 def test_null_pointers_are_bad_args(pkg):

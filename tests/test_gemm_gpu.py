@@ -123,6 +123,22 @@ def test_tile_and_stage_choices_agree_bitwise(pkg, orc, cuda):
         assert torch.equal(ops.d, ref), (tn, tk, s)
 
 
+@pytest.mark.parametrize("dtype,tile_k", [(0, 16), (0, 32), (1, 32), (1, 64)])
+@pytest.mark.parametrize("cta_group,tile_n", [(1, 256), (1, 64), (1, 16), (2, 256), (2, 512)])
+def test_narrow_tile_k_swizzle_modes(pkg, orc, cuda, dtype, tile_k, cta_group, tile_n):
+    """TILE_K below one 128-byte row (32- and 64-byte swizzle, the reference
+    sweep's bf16 TILE_K 16/32 and fp8 32/64) against the oracle, and bit-identical
+    to the 128-byte-row kernel: the MMAs walk K in the same 32-byte steps."""
+    m, n, k = 512, 1024, 328 if dtype == 0 else 336       # K tail inside the last stage
+    ops = make(pkg, dtype, m, n, k, cuda)
+    pkg.gemm(ops, cta_group=cta_group, tile_n=tile_n, tile_k=tile_k)
+    assert rel_err(orc, pkg, ops) <= TOL[dtype]
+    narrow = ops.d.clone()
+    ops.d.fill_(0)
+    pkg.gemm(ops, cta_group=1, tile_n=256, tile_k=64 if dtype == 0 else 128)
+    assert torch.equal(ops.d, narrow)
+
+
 def test_config2_bf16_8192_sampled(pkg, orc, cuda):
     """BASELINE config 2 (bf16 8192^3, 128x256x64, 4 stages), sampled fp64 check:
     a random 128 x 128 block plus two full rows and two full columns."""
