@@ -90,6 +90,7 @@ struct KernelParams {
   uint32_t stage_bytes;   // per CTA: A + B (+ scale factors)
   uint32_t a_atom_bytes, b_atom_bytes;
   uint32_t row_bytes;     // bytes of one operand row in a K atom: 128, 64 or 32 (the swizzle width)
+  int32_t cta_rows;       // A rows (accumulator rows) per CTA: 128, or 64 for a 1-SM TILE_M = 64
   uint32_t sf_stage_bytes;  // NVFP4: SFA + SFB bytes per stage per CTA
   uint32_t idesc;
   float alpha;
@@ -217,13 +218,16 @@ __global__ void __launch_bounds__(threads_for(BN), 1)
 gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ KernelParams p) {
-  constexpr int BM = 128;                 // A rows per CTA (= TMEM lanes)
+  // A rows per CTA.  128 fills the 128 TMEM lanes; a 1-SM TILE_M = 64 tile
+  // (M = 64 MMA) puts row r of the accumulator in lane 32*(r/16) + r%16, i.e.
+  // the first 16 lanes of each 32-lane quadrant.
+  const int BM = CG == 2 ? 128 : p.cta_rows;
   constexpr int BN_CTA = BN / CG;         // B rows per CTA
   constexpr int MMA_N = BN > 256 ? 256 : BN;  // N of one tcgen05.mma
   constexpr int N_SUB = BN / MMA_N;       // MMAs per K step (N halves of a 512-wide pair tile)
   constexpr int B_BOX = MMA_N / CG;       // B rows per CTA per N half (one TMA box)
   constexpr int EPI_WARPS = epi_warps_for(BN);
-  constexpr int MMA_M = BM * CG;
+  const int MMA_M = BM * CG;
   constexpr int KIND = DT == 0 ? 0 : 1;
   const int MAP_ELEMS_PER_ATOM = (int)p.row_bytes / (DT == 0 ? 2 : 1);  // tensor-map elements per atom row
   constexpr int SF_COLS_A = 4;            // TMEM columns of SFA per 64-element K step (NVFP4)
@@ -485,9 +489,10 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const bool ok = wait_bar<false>(tfull_bar + 8u * acc, acc_phase, ctl, ROLE_EPILOGUE, acc);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int64_t row = (int64_t)um * MMA_M + (int64_t)cta_rank * BM + 32 * q + lane;
+      const int q_rows = BM / 4;                  // accumulator rows in this warp's quadrant
+      const int64_t row = (int64_t)um * MMA_M + (int64_t)cta_rank * BM + q_rows * (int)q + lane;
       const int64_t n0 = (int64_t)un * BN;
-      const bool row_ok = row < p.m;
+      const bool row_ok = (int)lane < q_rows && row < p.m;
       __nv_bfloat16* const dptr = p.d + row;
       const uint32_t t_row = tmem_base + ((32u * q) << 16) + (uint32_t)(acc * BN);
       if constexpr (COLS % 32 == 0) {
@@ -598,7 +603,12 @@ int resolve(const GemmArgs* a, Resolved& r) {
   r.cluster_m = a->cluster_m == 0 ? r.cg : a->cluster_m;
   if (r.cluster_m != r.cg) FAIL("cluster_m %d unsupported (must equal cta_group)", r.cluster_m);
   r.bm = 128 * r.cg;
-  if (a->tile_m != 0 && a->tile_m != r.bm) FAIL("tile_m %d unsupported for cta_group %d (need %d)", a->tile_m, r.cg, r.bm);
+  if (r.cg == 1 && a->tile_m == 64) {
+    if (r.dt == 2) FAIL("tile_m 64 unsupported for NVFP4 (scale atoms are 128 rows)");
+    r.bm = 64;
+  }
+  if (a->tile_m != 0 && a->tile_m != r.bm)
+    FAIL("tile_m %d unsupported for cta_group %d (need %d%s)", a->tile_m, r.cg, r.bm, r.cg == 1 ? " or 64" : "");
   r.bn = a->tile_n == 0 ? 256 : a->tile_n;
   if (!supported_bn(r.cg, r.bn)) FAIL("tile_n %d unsupported for cta_group %d", r.bn, r.cg);
   const int ae = atom_elems(r.dt);
@@ -633,7 +643,7 @@ int resolve(const GemmArgs* a, Resolved& r) {
     if (((uintptr_t)a->sfa | (uintptr_t)a->sfb) & 15) FAIL("sfa/sfb must be 16-byte aligned");
   }
 
-  r.a_atom_bytes = 128u * r.row_bytes;
+  r.a_atom_bytes = (uint32_t)(r.bm / r.cg) * r.row_bytes;
   r.b_atom_bytes = (uint32_t)(r.bn / r.cg) * r.row_bytes;
   r.sf_stage_bytes = 0;
   if (r.dt == 2) {
@@ -778,7 +788,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   const uint64_t inner_k = (uint64_t)(r.dt == 2 ? a.k / 2 : a.k);       // tensor-map elements along K
   const uint32_t box_inner = bf ? r.row_bytes / 2 : r.row_bytes;
   if (!encode_2d(&tma_a, a.a, t, inner_k, (uint64_t)a.m, (uint64_t)(a.lda * eb_num / eb_den), box_inner,
-                 128u, r.row_bytes))
+                 (uint32_t)(r.bm / r.cg), r.row_bytes))
     return GEMM_ERR_CANNOT_IMPLEMENT;
   if (!encode_2d(&tmb_b, a.b, t, inner_k, (uint64_t)a.n, (uint64_t)(a.ldb * eb_num / eb_den), box_inner,
                  (uint32_t)((r.bn > 256 ? 256 : r.bn) / r.cg), r.row_bytes))
@@ -792,6 +802,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   p.raster_group = r.raster_group; p.tmem_cols = r.tmem_cols;
   p.stage_bytes = r.stage_bytes; p.a_atom_bytes = r.a_atom_bytes; p.b_atom_bytes = r.b_atom_bytes;
   p.row_bytes = r.row_bytes;
+  p.cta_rows = r.bm / r.cg;
   p.sf_stage_bytes = r.sf_stage_bytes;
   p.idesc = make_idesc(r.dt, r.bm, r.bn > 256 ? 256 : r.bn);
   p.num_acc = r.num_acc;

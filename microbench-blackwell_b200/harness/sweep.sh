@@ -11,9 +11,9 @@
 # (cutlass_gemm_mainloop/sweep.sh:85-149).  The harness is host-only C++ over
 # the prebuilt library, so a build takes about a second instead of a minute.
 #
-# Tile lists: the reference's BF16 and FP8 lists (sweep.sh:28-65; TILE_M 64
-# and TILE_K below one 128-byte swizzle atom are reported as FAILED rows by
-# this library) plus NVFP4 (DTYPE_ID=2) and CTA-pair (TILE_M=256) tiles.
+# Tile lists: the reference's BF16 and FP8 lists (sweep.sh:28-65: TILE_M 64
+# and 128, TILE_K down to one MMA K step -- 32- and 64-byte swizzle rows) plus
+# NVFP4 (DTYPE_ID=2) and CTA-pair (TILE_M=256) tiles.
 #   SWEEP=focus (default: the 128/256-row tiles at the default TILE_K)
 #   SWEEP=full  (every reference tile)
 set -e

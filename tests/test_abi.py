@@ -108,6 +108,20 @@ def test_narrow_tile_k_uses_narrow_swizzle(pkg, dtype, tile_k, row_bytes):
     assert info.smem_bytes_per_stage == (128 + 256) * row_bytes
 
 
+@pytest.mark.parametrize("dtype,tile_k", [("bf16", 64), ("fp8", 128), ("bf16", 16)])
+def test_tile_m_64_is_a_1sm_tile(pkg, dtype, tile_k):
+    """TILE_M = 64 (the reference sweeps 64 and 128) is an M = 64 MMA on one SM."""
+    dt = pkg.BF16 if dtype == "bf16" else pkg.FP8_E4M3
+    rc, info = pkg.query(_args(pkg, dtype=dt, tile_m=64, tile_n=128, tile_k=tile_k))
+    assert rc == pkg.OK, info.reason
+    assert info.tile_m == 64 and info.cta_group == 1
+    row_bytes = min(128, tile_k * (2 if dtype == "bf16" else 1))
+    assert info.smem_bytes_per_stage == (64 + 128) * row_bytes * max(1, tile_k * (2 if dtype == "bf16" else 1) // 128)
+    assert info.num_tiles == (8192 // 64) * (8192 // 128)
+    rc, info = pkg.query(_args(pkg, dtype=dt, tile_m=64, cta_group=2, tile_n=256, tile_k=tile_k))
+    assert rc == pkg.ERR_CANNOT_IMPLEMENT and b"tile_m" in info.reason
+
+
 def test_null_pointers_are_bad_args(pkg):
     rc, _ = pkg.query(_args(pkg, a=None))
     assert rc == pkg.ERR_BAD_ARGS

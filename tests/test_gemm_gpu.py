@@ -139,6 +139,30 @@ def test_narrow_tile_k_swizzle_modes(pkg, orc, cuda, dtype, tile_k, cta_group, t
     assert torch.equal(ops.d, narrow)
 
 
+def test_tile_m_64_identity_kat(pkg, orc, cuda):
+    """M = 64 accumulator layout: with A = I, D = B^T exactly (each product
+    is one bf16 value times 1), so every row and column must land in place."""
+    m, n, k = 192, 256, 192
+    ops = make(pkg, pkg.BF16, m, n, k, cuda)
+    ops.a.copy_(torch.eye(m, k, dtype=torch.bfloat16, device=cuda))
+    pkg.gemm(ops, tile_m=64, tile_n=128, tile_k=64)
+    assert torch.equal(ops.d, ops.b[:, :m].contiguous())   # D^T storage (n, m) = B[:, :m]
+
+
+@pytest.mark.parametrize("dtype,tile_k", [(0, 64), (0, 16), (1, 128), (1, 32)])
+@pytest.mark.parametrize("m,n,k,tile_n", [(200, 300, 320, 256), (448, 512, 512, 128), (64, 16, 1024, 16)])
+def test_tile_m_64_matches_oracle_and_128_bitwise(pkg, orc, cuda, dtype, tile_k, m, n, k, tile_n):
+    """TILE_M = 64 (partial M and N tiles included) against the oracle, and
+    bit-identical to the TILE_M = 128 kernel."""
+    ops = make(pkg, dtype, m, n, k, cuda)
+    pkg.gemm(ops, tile_m=64, tile_n=tile_n, tile_k=tile_k)
+    assert rel_err(orc, pkg, ops) <= TOL[dtype]
+    d64 = ops.d.clone()
+    ops.d.fill_(0)
+    pkg.gemm(ops, tile_n=256, tile_k=64 if dtype == 0 else 128)
+    assert torch.equal(ops.d, d64)
+
+
 def test_config2_bf16_8192_sampled(pkg, orc, cuda):
     """BASELINE config 2 (bf16 8192^3, 128x256x64, 4 stages), sampled fp64 check:
     a random 128 x 128 block plus two full rows and two full columns."""
