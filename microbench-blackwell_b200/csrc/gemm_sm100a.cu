@@ -58,7 +58,7 @@ constexpr unsigned kTraceRegion = 1u << 14;
 __device__ unsigned long long g_trace_log[4 * kTraceRegion];
 #define TRACE_EVENT(role, kind, stage)                                                     \
   do {                                                                                     \
-    if (blockIdx.x == 0 && trace_i < kTraceRegion)                                         \
+    if (blockIdx.x == 0 && (threadIdx.x & 31u) == 0 && trace_i < kTraceRegion)            \
       g_trace_log[(role) * kTraceRegion + trace_i++] =                                     \
           ((unsigned long long)clock64() << 16) | ((role) << 12) | ((kind) << 8) | ((stage) & 0xFF); \
   } while (0)
@@ -249,7 +249,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   const uint32_t abort_flag = tmem_slot + 4u;
   uint32_t* const tmem_slot_ptr = reinterpret_cast<uint32_t*>(base_ptr + (tmem_slot - base));
 
-  const uint32_t warp = threadIdx.x >> 5;
+  const uint32_t warp = __shfl_sync(0xffffffffu, threadIdx.x >> 5, 0);   // warp-uniform
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t cta_rank = CG == 2 ? cluster_ctarank() : 0u;
   const bool leader = cta_rank == 0;
@@ -278,7 +278,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   tc_fence_before();
   if constexpr (CG == 2) { cluster_arrive(); cluster_wait(); } else { __syncthreads(); }
   tc_fence_after();
-  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot_ptr);
+  const uint32_t tmem_base = __shfl_sync(0xffffffffu, *reinterpret_cast<volatile uint32_t*>(tmem_slot_ptr), 0);
 
   SharedCtl ctl;
   ctl.abort_addr = abort_flag;
@@ -288,7 +288,9 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && !(p.flags & GEMM_FLAG_INJECT_STALL)) {
+    // The whole warp runs the loop so every address below is warp-uniform
+    // (uniform registers); one elected lane issues the loads.
+    if (!(p.flags & GEMM_FLAG_INJECT_STALL)) {
       const uint64_t policy = policy_evict_normal();
       unsigned trace_i = 0;
       (void)trace_i;
@@ -309,12 +311,15 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       };
       auto pf_step = [&]() {
         if (pf_u >= p.num_units) return;
-        for (int ka = 0; ka < p.atoms; ++ka) {
-          const int32_t x = (pf_kb * p.atoms + ka) * MAP_ELEMS_PER_ATOM;
-          tma_prefetch_l2_2d(&tmap_a, x, pf_m0);
+        if (elect_one()) {
+          for (int ka = 0; ka < p.atoms; ++ka) {
+            const int32_t x = (pf_kb * p.atoms + ka) * MAP_ELEMS_PER_ATOM;
+            tma_prefetch_l2_2d(&tmap_a, x, pf_m0);
 #pragma unroll
-          for (int h = 0; h < N_SUB; ++h) tma_prefetch_l2_2d(&tmap_b, x, pf_n0 + h * MMA_N);
+            for (int h = 0; h < N_SUB; ++h) tma_prefetch_l2_2d(&tmap_b, x, pf_n0 + h * MMA_N);
+          }
         }
+        __syncwarp();
         if (++pf_kb == p.num_k_blocks) {
           pf_kb = 0;
           pf_u += num_pairs;
@@ -331,45 +336,49 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const int32_t m0 = um * MMA_M + (int32_t)cta_rank * BM;
         const int32_t n0 = un * BN + (int32_t)cta_rank * B_BOX;
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          if (!wait_bar<false>(empty_bar + 8u * stage, phase ^ 1u, ctl, ROLE_PRODUCER, stage)) { ok = false; break; }
+          const bool w = wait_bar<false>(empty_bar + 8u * stage, phase ^ 1u, ctl, ROLE_PRODUCER, stage);
+          if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
           TRACE_EVENT(1u, 1u, stage);
           if (p.l2_prefetch > 0) pf_step();
           const uint32_t sbase = ring + (uint32_t)stage * p.stage_bytes;
           const uint32_t fb = full_bar + 8u * stage;
-          if (leader) mbar_arrive_expect_tx(fb, tx_bytes);
           const uint32_t target = CG == 2 ? leader_full + 8u * stage : fb;
-          for (int ka = 0; ka < p.atoms; ++ka) {
-            const int32_t x = (kb * p.atoms + ka) * MAP_ELEMS_PER_ATOM;
-            const uint32_t a_dst = sbase + (uint32_t)ka * p.a_atom_bytes;
-            const uint32_t b_dst = sbase + (uint32_t)p.atoms * p.a_atom_bytes + (uint32_t)ka * p.b_atom_bytes;
-            if constexpr (CG == 2) {
-              tma_load_2d_pair(a_dst, &tmap_a, target, x, m0, policy);
+          if (elect_one()) {
+            if (leader) mbar_arrive_expect_tx(fb, tx_bytes);
+            for (int ka = 0; ka < p.atoms; ++ka) {
+              const int32_t x = (kb * p.atoms + ka) * MAP_ELEMS_PER_ATOM;
+              const uint32_t a_dst = sbase + (uint32_t)ka * p.a_atom_bytes;
+              const uint32_t b_dst = sbase + (uint32_t)p.atoms * p.a_atom_bytes + (uint32_t)ka * p.b_atom_bytes;
+              if constexpr (CG == 2) {
+                tma_load_2d_pair(a_dst, &tmap_a, target, x, m0, policy);
 #pragma unroll
-              for (int h = 0; h < N_SUB; ++h)
-                tma_load_2d_pair(b_dst + (uint32_t)(h * B_BOX) * p.row_bytes, &tmap_b, target, x, n0 + h * MMA_N, policy);
-            } else {
-              tma_load_2d(a_dst, &tmap_a, target, x, m0, policy);
+                for (int h = 0; h < N_SUB; ++h)
+                  tma_load_2d_pair(b_dst + (uint32_t)(h * B_BOX) * p.row_bytes, &tmap_b, target, x, n0 + h * MMA_N, policy);
+              } else {
+                tma_load_2d(a_dst, &tmap_a, target, x, m0, policy);
 #pragma unroll
-              for (int h = 0; h < N_SUB; ++h)
-                tma_load_2d(b_dst + (uint32_t)(h * B_BOX) * p.row_bytes, &tmap_b, target, x, n0 + h * MMA_N, policy);
+                for (int h = 0; h < N_SUB; ++h)
+                  tma_load_2d(b_dst + (uint32_t)(h * B_BOX) * p.row_bytes, &tmap_b, target, x, n0 + h * MMA_N, policy);
+              }
+            }
+            if constexpr (DT == 2) {
+              // Scale factors: one 512-byte atom (128 rows x 4 scales) per 64 K
+              // elements; a stage covers atoms*4 of them for A, and for B
+              // ceil(BN_CTA/128) row blocks each.
+              const uint32_t sf_base = sbase + (uint32_t)p.atoms * (p.a_atom_bytes + p.b_atom_bytes);
+              const int kq0 = kb * p.atoms * 4;
+              const int nsf = p.atoms * 4;
+              const uint8_t* sfa_src = p.sfa + ((int64_t)(m0 / 128) * p.sf_kblocks + kq0) * 512;
+              bulk_load(sf_base, sfa_src, (uint32_t)nsf * 512u, target, policy);
+              constexpr int B_BLOCKS = (BN_CTA + 127) / 128;
+#pragma unroll
+              for (int bb = 0; bb < B_BLOCKS; ++bb) {
+                const uint8_t* sfb_src = p.sfb + ((int64_t)(n0 / 128 + bb) * p.sf_kblocks + kq0) * 512;
+                bulk_load(sf_base + (uint32_t)nsf * 512u * (1 + bb), sfb_src, (uint32_t)nsf * 512u, target, policy);
+              }
             }
           }
-          if constexpr (DT == 2) {
-            // Scale factors: one 512-byte atom (128 rows x 4 scales) per 64 K
-            // elements; a stage covers atoms*4 of them for A, and for B
-            // ceil(BN_CTA/128) row blocks each.
-            const uint32_t sf_base = sbase + (uint32_t)p.atoms * (p.a_atom_bytes + p.b_atom_bytes);
-            const int kq0 = kb * p.atoms * 4;
-            const int nsf = p.atoms * 4;
-            const uint8_t* sfa_src = p.sfa + ((int64_t)(m0 / 128) * p.sf_kblocks + kq0) * 512;
-            bulk_load(sf_base, sfa_src, (uint32_t)nsf * 512u, target, policy);
-            constexpr int B_BLOCKS = (BN_CTA + 127) / 128;
-#pragma unroll
-            for (int bb = 0; bb < B_BLOCKS; ++bb) {
-              const uint8_t* sfb_src = p.sfb + ((int64_t)(n0 / 128 + bb) * p.sf_kblocks + kq0) * 512;
-              bulk_load(sf_base + (uint32_t)nsf * 512u * (1 + bb), sfb_src, (uint32_t)nsf * 512u, target, policy);
-            }
-          }
+          __syncwarp();
           TRACE_EVENT(1u, 2u, stage);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -387,7 +396,11 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && leader) {
+    // Converged warp: descriptors and addresses are warp-uniform; one lane,
+    // elected once, issues every tcgen05 op, so its commits track all of its
+    // MMAs.
+    if (leader) {
+      const bool mma_lane = elect_one();
       unsigned trace_i = 0;
       (void)trace_i;
       int stage = 0;
@@ -404,11 +417,13 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const int k_steps = (int)(row_b / 32u);   // 32 bytes of K per MMA
       const int n_acc = p.num_acc;
       for (int u = pair; u < n_units && ok; u += num_pairs) {
-        if (!wait_bar<CG == 2>(tempty_bar + 8u * acc, acc_phase ^ 1u, ctl, ROLE_MMA, 0x80u | acc)) { ok = false; break; }
+        const bool wt = wait_bar<CG == 2>(tempty_bar + 8u * acc, acc_phase ^ 1u, ctl, ROLE_MMA, 0x80u | acc);
+        if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < n_kb; ++kb) {
-          if (!wait_bar<CG == 2>(full_bar + 8u * stage, phase, ctl, ROLE_MMA, stage)) { ok = false; break; }
+          const bool w = wait_bar<CG == 2>(full_bar + 8u * stage, phase, ctl, ROLE_MMA, stage);
+          if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
           TRACE_EVENT(2u, 1u, stage);
           tc_fence_after();
           const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
@@ -420,56 +435,68 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const int nsf = n_atoms * 4;
             const uint32_t sfa_t = tmem_base + (uint32_t)(n_acc * BN);
             const uint32_t sfb_t = sfa_t + (uint32_t)nsf * SF_COLS_A;
-            for (int q = 0; q < nsf; ++q) {
-              tmem_cp_32x128b_warpx4<CG>(sfa_t + (uint32_t)q * SF_COLS_A, plain_desc(sf_base + (uint32_t)q * 512u));
-              for (int bb = 0; bb < SF_COLS_B / 4; ++bb)
-                tmem_cp_32x128b_warpx4<CG>(sfb_t + (uint32_t)q * SF_COLS_B + 4u * bb,
-                                           plain_desc(sf_base + (uint32_t)nsf * 512u * (1 + bb) + (uint32_t)q * 512u));
-            }
-            for (int ka = 0; ka < n_atoms; ++ka) {
-              const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, row_b);
-              const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, row_b);
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                const int q = ka * 4 + kk;
-                mma_nvf4<CG>(d_tmem, ad + 2u * kk, bd + 2u * kk, idesc,
-                             sfa_t + (uint32_t)q * SF_COLS_A, sfb_t + (uint32_t)q * SF_COLS_B,
-                             (kb | ka | kk) != 0);
+            if (mma_lane) {
+              for (int q = 0; q < nsf; ++q) {
+                tmem_cp_32x128b_warpx4<CG>(sfa_t + (uint32_t)q * SF_COLS_A, plain_desc(sf_base + (uint32_t)q * 512u));
+                for (int bb = 0; bb < SF_COLS_B / 4; ++bb)
+                  tmem_cp_32x128b_warpx4<CG>(sfb_t + (uint32_t)q * SF_COLS_B + 4u * bb,
+                                             plain_desc(sf_base + (uint32_t)nsf * 512u * (1 + bb) + (uint32_t)q * 512u));
               }
+              for (int ka = 0; ka < n_atoms; ++ka) {
+                const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, row_b);
+                const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, row_b);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  const int q = ka * 4 + kk;
+                  mma_nvf4<CG>(d_tmem, ad + 2u * kk, bd + 2u * kk, idesc,
+                               sfa_t + (uint32_t)q * SF_COLS_A, sfb_t + (uint32_t)q * SF_COLS_B,
+                               (kb | ka | kk) != 0);
+                }
+              }
+              if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3); else mma_commit(empty_bar + 8u * stage);
             }
           } else {
-            for (int ka = 0; ka < n_atoms; ++ka) {
-              const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, row_b);
-              const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, row_b);
-              if (k_steps == 4) {   // 128-byte rows: the fully unrolled common case
+            if (mma_lane) {
+              for (int ka = 0; ka < n_atoms; ++ka) {
+                const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, row_b);
+                const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, row_b);
+                if (k_steps == 4) {   // 128-byte rows: the fully unrolled common case
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
+                  for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-                  for (int h = 0; h < N_SUB; ++h)
-                    mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
-                                     bd + (uint64_t)((h * B_BOX * 128) >> 4) + 2u * kk, idesc, (kb | ka | kk) != 0);
-              } else {              // 64- or 32-byte rows (narrow TILE_K): 2 or 1 K steps
-                for (int kk = 0; kk < k_steps; ++kk)
+                    for (int h = 0; h < N_SUB; ++h)
+                      mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
+                                       bd + (uint64_t)((h * B_BOX * 128) >> 4) + 2u * kk, idesc, (kb | ka | kk) != 0);
+                } else {              // 64- or 32-byte rows (narrow TILE_K): 2 or 1 K steps
+                  for (int kk = 0; kk < k_steps; ++kk)
 #pragma unroll
-                  for (int h = 0; h < N_SUB; ++h)
-                    mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
-                                     bd + (uint64_t)(((uint32_t)(h * B_BOX) * row_b) >> 4) + 2u * kk, idesc,
-                                     (kb | ka | kk) != 0);
+                    for (int h = 0; h < N_SUB; ++h)
+                      mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
+                                       bd + (uint64_t)(((uint32_t)(h * B_BOX) * row_b) >> 4) + 2u * kk, idesc,
+                                       (kb | ka | kk) != 0);
+                }
               }
+              if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3); else mma_commit(empty_bar + 8u * stage);
             }
           }
-          if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3); else mma_commit(empty_bar + 8u * stage);
+          __syncwarp();
           TRACE_EVENT(2u, 2u, stage);
           issued = true;
           if (++stage == n_stages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3); else mma_commit(tfull_bar + 8u * acc);
+        if (mma_lane) {
+          if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3); else mma_commit(tfull_bar + 8u * acc);
+        }
+        __syncwarp();
         if (++acc == n_acc) { acc = 0; acc_phase ^= 1u; }
       }
       if (!ok && issued) {
         // Wait (bounded) until every MMA already issued has finished with TMEM.
-        if constexpr (CG == 2) mma_commit_pair(drain_bar, 0x1); else mma_commit(drain_bar);
+        if (mma_lane) {
+          if constexpr (CG == 2) mma_commit_pair(drain_bar, 0x1); else mma_commit(drain_bar);
+        }
+        __syncwarp();
         drain_wait(drain_bar, 0, 100000000ull);
       }
     }
