@@ -68,6 +68,9 @@ __device__ unsigned long long g_trace_log[4 * kTraceRegion];
 
 namespace {
 
+template <int V>
+struct IntC { static constexpr int value = V; };
+
 // Threads per CTA: producer warp + MMA warp + EPI_WARPS epilogue warps.
 __host__ __device__ constexpr int epi_warps_for(int bn) { return bn > 256 ? 8 : 4; }
 __host__ __device__ constexpr int threads_for(int bn) { return 64 + 32 * epi_warps_for(bn); }
@@ -229,7 +232,6 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   constexpr int EPI_WARPS = epi_warps_for(BN);
   const int MMA_M = BM * CG;
   constexpr int KIND = DT == 0 ? 0 : 1;
-  const int MAP_ELEMS_PER_ATOM = (int)p.row_bytes / (DT == 0 ? 2 : 1);  // tensor-map elements per atom row
   constexpr int SF_COLS_A = 4;            // TMEM columns of SFA per 64-element K step (NVFP4)
   constexpr int SF_COLS_B = ((BN + 127) / 128) * 4;
 
@@ -286,16 +288,37 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   ctl.timeout_ns = p.timeout_ns;
   ctl.status = p.status;
 
+  // Shape of one pipeline stage as compile-time constants: NA K atoms per
+  // stage, KS MMAs (32-byte K steps) per atom row of KS * 32 bytes.  The
+  // producer and MMA loops are instantiated per shape and dispatched once,
+  // so no runtime loop or branch on the tile shape sits in the k-block loop.
+  auto with_stage_shape = [&](auto&& body) {
+    switch (p.atoms * 8 + (int)(p.row_bytes / 32u)) {
+      case 1 * 8 + 4: body(IntC<1>{}, IntC<4>{}); break;
+      case 2 * 8 + 4: body(IntC<2>{}, IntC<4>{}); break;
+      case 4 * 8 + 4: body(IntC<4>{}, IntC<4>{}); break;
+      case 1 * 8 + 2: body(IntC<1>{}, IntC<2>{}); break;
+      case 1 * 8 + 1: body(IntC<1>{}, IntC<1>{}); break;
+      default: break;   // the host admits no other shape
+    }
+  };
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // The whole warp runs the loop so every address below is warp-uniform
-    // (uniform registers); one elected lane issues the loads.
-    if (!(p.flags & GEMM_FLAG_INJECT_STALL)) {
+    // The whole warp runs the loop so every address below is warp-uniform;
+    // the loads are predicated on one elected lane (no branch around them).
+    if (!(p.flags & GEMM_FLAG_INJECT_STALL)) with_stage_shape([&](auto na_c, auto ks_c) {
+      constexpr int NA = decltype(na_c)::value;
+      constexpr uint32_t RB = (uint32_t)decltype(ks_c)::value * 32u;   // bytes per atom row
+      constexpr int ELEMS = (int)RB / (DT == 0 ? 2 : 1);                 // tensor-map elements per atom row
+      const uint32_t issue = elect_one() ? 1u : 0u;
       const uint64_t policy = policy_evict_normal();
       unsigned trace_i = 0;
       (void)trace_i;
       const uint32_t leader_full = CG == 2 ? mapa_shared(full_bar, 0) : full_bar;
       const uint32_t tx_bytes = p.stage_bytes * CG;
+      const uint32_t st_bytes = p.stage_bytes, a_bytes = p.a_atom_bytes, b_bytes = p.b_atom_bytes;
+      const int n_kb = p.num_k_blocks, n_stages = p.stages;
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
@@ -311,16 +334,14 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       };
       auto pf_step = [&]() {
         if (pf_u >= p.num_units) return;
-        if (elect_one()) {
-          for (int ka = 0; ka < p.atoms; ++ka) {
-            const int32_t x = (pf_kb * p.atoms + ka) * MAP_ELEMS_PER_ATOM;
-            tma_prefetch_l2_2d(&tmap_a, x, pf_m0);
 #pragma unroll
-            for (int h = 0; h < N_SUB; ++h) tma_prefetch_l2_2d(&tmap_b, x, pf_n0 + h * MMA_N);
-          }
+        for (int ka = 0; ka < NA; ++ka) {
+          const int32_t x = (pf_kb * NA + ka) * ELEMS;
+          tma_prefetch_l2_2d(&tmap_a, x, pf_m0, issue);
+#pragma unroll
+          for (int h = 0; h < N_SUB; ++h) tma_prefetch_l2_2d(&tmap_b, x, pf_n0 + h * MMA_N, issue);
         }
-        __syncwarp();
-        if (++pf_kb == p.num_k_blocks) {
+        if (++pf_kb == n_kb) {
           pf_kb = 0;
           pf_u += num_pairs;
           if (pf_u < p.num_units) pf_coords();
@@ -335,72 +356,72 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         unit_coords(u, p, um, un);
         const int32_t m0 = um * MMA_M + (int32_t)cta_rank * BM;
         const int32_t n0 = un * BN + (int32_t)cta_rank * B_BOX;
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        for (int kb = 0; kb < n_kb; ++kb) {
           const bool w = wait_bar<false>(empty_bar + 8u * stage, phase ^ 1u, ctl, ROLE_PRODUCER, stage);
           if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
           TRACE_EVENT(1u, 1u, stage);
           if (p.l2_prefetch > 0) pf_step();
-          const uint32_t sbase = ring + (uint32_t)stage * p.stage_bytes;
+          const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
           const uint32_t fb = full_bar + 8u * stage;
           const uint32_t target = CG == 2 ? leader_full + 8u * stage : fb;
-          if (elect_one()) {
-            if (leader) mbar_arrive_expect_tx(fb, tx_bytes);
-            for (int ka = 0; ka < p.atoms; ++ka) {
-              const int32_t x = (kb * p.atoms + ka) * MAP_ELEMS_PER_ATOM;
-              const uint32_t a_dst = sbase + (uint32_t)ka * p.a_atom_bytes;
-              const uint32_t b_dst = sbase + (uint32_t)p.atoms * p.a_atom_bytes + (uint32_t)ka * p.b_atom_bytes;
+          mbar_arrive_expect_tx(fb, tx_bytes, leader ? issue : 0u);
+#pragma unroll
+          for (int ka = 0; ka < NA; ++ka) {
+            const int32_t x = (kb * NA + ka) * ELEMS;
+            const uint32_t a_dst = sbase + (uint32_t)ka * a_bytes;
+            const uint32_t b_dst = sbase + (uint32_t)NA * a_bytes + (uint32_t)ka * b_bytes;
+#pragma unroll
+            for (int h = 0; h < N_SUB; ++h) {
               if constexpr (CG == 2) {
-                tma_load_2d_pair(a_dst, &tmap_a, target, x, m0, policy);
-#pragma unroll
-                for (int h = 0; h < N_SUB; ++h)
-                  tma_load_2d_pair(b_dst + (uint32_t)(h * B_BOX) * p.row_bytes, &tmap_b, target, x, n0 + h * MMA_N, policy);
+                if (h == 0) tma_load_2d_pair(a_dst, &tmap_a, target, x, m0, policy, issue);
+                tma_load_2d_pair(b_dst + (uint32_t)(h * B_BOX) * RB, &tmap_b, target, x, n0 + h * MMA_N, policy, issue);
               } else {
-                tma_load_2d(a_dst, &tmap_a, target, x, m0, policy);
-#pragma unroll
-                for (int h = 0; h < N_SUB; ++h)
-                  tma_load_2d(b_dst + (uint32_t)(h * B_BOX) * p.row_bytes, &tmap_b, target, x, n0 + h * MMA_N, policy);
-              }
-            }
-            if constexpr (DT == 2) {
-              // Scale factors: one 512-byte atom (128 rows x 4 scales) per 64 K
-              // elements; a stage covers atoms*4 of them for A, and for B
-              // ceil(BN_CTA/128) row blocks each.
-              const uint32_t sf_base = sbase + (uint32_t)p.atoms * (p.a_atom_bytes + p.b_atom_bytes);
-              const int kq0 = kb * p.atoms * 4;
-              const int nsf = p.atoms * 4;
-              const uint8_t* sfa_src = p.sfa + ((int64_t)(m0 / 128) * p.sf_kblocks + kq0) * 512;
-              bulk_load(sf_base, sfa_src, (uint32_t)nsf * 512u, target, policy);
-              constexpr int B_BLOCKS = (BN_CTA + 127) / 128;
-#pragma unroll
-              for (int bb = 0; bb < B_BLOCKS; ++bb) {
-                const uint8_t* sfb_src = p.sfb + ((int64_t)(n0 / 128 + bb) * p.sf_kblocks + kq0) * 512;
-                bulk_load(sf_base + (uint32_t)nsf * 512u * (1 + bb), sfb_src, (uint32_t)nsf * 512u, target, policy);
+                if (h == 0) tma_load_2d(a_dst, &tmap_a, target, x, m0, policy, issue);
+                tma_load_2d(b_dst + (uint32_t)(h * B_BOX) * RB, &tmap_b, target, x, n0 + h * MMA_N, policy, issue);
               }
             }
           }
-          __syncwarp();
+          if constexpr (DT == 2) {
+            // Scale factors: one 512-byte atom (128 rows x 4 scales) per 64 K
+            // elements; a stage covers NA*4 of them for A, and for B
+            // ceil(BN_CTA/128) row blocks each.
+            const uint32_t sf_base = sbase + (uint32_t)NA * (a_bytes + b_bytes);
+            const int kq0 = kb * NA * 4;
+            constexpr int NSF = NA * 4;
+            const uint8_t* sfa_src = p.sfa + ((int64_t)(m0 / 128) * p.sf_kblocks + kq0) * 512;
+            bulk_load(sf_base, sfa_src, (uint32_t)NSF * 512u, target, policy, issue);
+            constexpr int B_BLOCKS = (BN_CTA + 127) / 128;
+#pragma unroll
+            for (int bb = 0; bb < B_BLOCKS; ++bb) {
+              const uint8_t* sfb_src = p.sfb + ((int64_t)(n0 / 128 + bb) * p.sf_kblocks + kq0) * 512;
+              bulk_load(sf_base + (uint32_t)NSF * 512u * (1 + bb), sfb_src, (uint32_t)NSF * 512u, target, policy, issue);
+            }
+          }
           TRACE_EVENT(1u, 2u, stage);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+          if (++stage == n_stages) { stage = 0; phase ^= 1u; }
         }
       }
       if (!ok && CG == 1) {
         // Let every load already issued land before the CTA may exit.
-        for (int s = 0; s < p.stages; ++s)
+        for (int s = 0; s < n_stages; ++s)
           if (issued_mask & (1u << s)) drain_wait(full_bar + 8u * s, (issued_parity >> s) & 1u, 100000000ull);
       } else if (!ok) {
         const uint64_t t0 = globaltimer_ns();
         while (globaltimer_ns() - t0 < 2000000ull) {}
       }
-    }
+    });
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Converged warp: descriptors and addresses are warp-uniform; one lane,
-    // elected once, issues every tcgen05 op, so its commits track all of its
-    // MMAs.
-    if (leader) {
-      const bool mma_lane = elect_one();
+    // Converged warp: descriptors and addresses are warp-uniform; every
+    // tcgen05 op is predicated on one lane, elected once, so its commits
+    // track all of its MMAs.
+    if (leader) with_stage_shape([&](auto na_c, auto ks_c) {
+      constexpr int NA = decltype(na_c)::value;
+      constexpr int KS = decltype(ks_c)::value;
+      constexpr uint32_t RB = (uint32_t)KS * 32u;
+      const uint32_t issue = elect_one() ? 1u : 0u;
       unsigned trace_i = 0;
       (void)trace_i;
       int stage = 0;
@@ -410,11 +431,9 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       bool ok = true;
       bool issued = false;
       // Loop-invariant parameters in registers.
-      const int n_units = p.num_units, n_kb = p.num_k_blocks, n_stages = p.stages, n_atoms = p.atoms;
+      const int n_units = p.num_units, n_kb = p.num_k_blocks, n_stages = p.stages;
       const uint32_t st_bytes = p.stage_bytes, a_bytes = p.a_atom_bytes, b_bytes = p.b_atom_bytes;
       const uint32_t idesc = p.idesc;
-      const uint32_t row_b = p.row_bytes;
-      const int k_steps = (int)(row_b / 32u);   // 32 bytes of K per MMA
       const int n_acc = p.num_acc;
       for (int u = pair; u < n_units && ok; u += num_pairs) {
         const bool wt = wait_bar<CG == 2>(tempty_bar + 8u * acc, acc_phase ^ 1u, ctl, ROLE_MMA, 0x80u | acc);
@@ -427,79 +446,66 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           TRACE_EVENT(2u, 1u, stage);
           tc_fence_after();
           const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
-          const uint32_t bbase = sbase + (uint32_t)n_atoms * a_bytes;
+          const uint32_t bbase = sbase + (uint32_t)NA * a_bytes;
           if constexpr (DT == 2) {
             // Copy this stage's scale factors into TMEM (columns after the
-            // two accumulators), then issue the block-scaled MMAs.
-            const uint32_t sf_base = bbase + (uint32_t)n_atoms * b_bytes;
-            const int nsf = n_atoms * 4;
+            // accumulators), then issue the block-scaled MMAs.
+            const uint32_t sf_base = bbase + (uint32_t)NA * b_bytes;
+            constexpr int NSF = NA * 4;
             const uint32_t sfa_t = tmem_base + (uint32_t)(n_acc * BN);
-            const uint32_t sfb_t = sfa_t + (uint32_t)nsf * SF_COLS_A;
-            if (mma_lane) {
-              for (int q = 0; q < nsf; ++q) {
-                tmem_cp_32x128b_warpx4<CG>(sfa_t + (uint32_t)q * SF_COLS_A, plain_desc(sf_base + (uint32_t)q * 512u));
-                for (int bb = 0; bb < SF_COLS_B / 4; ++bb)
-                  tmem_cp_32x128b_warpx4<CG>(sfb_t + (uint32_t)q * SF_COLS_B + 4u * bb,
-                                             plain_desc(sf_base + (uint32_t)nsf * 512u * (1 + bb) + (uint32_t)q * 512u));
-              }
-              for (int ka = 0; ka < n_atoms; ++ka) {
-                const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, row_b);
-                const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, row_b);
+            const uint32_t sfb_t = sfa_t + (uint32_t)NSF * SF_COLS_A;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                  const int q = ka * 4 + kk;
-                  mma_nvf4<CG>(d_tmem, ad + 2u * kk, bd + 2u * kk, idesc,
-                               sfa_t + (uint32_t)q * SF_COLS_A, sfb_t + (uint32_t)q * SF_COLS_B,
-                               (kb | ka | kk) != 0);
-                }
+            for (int q = 0; q < NSF; ++q) {
+              tmem_cp_32x128b_warpx4<CG>(sfa_t + (uint32_t)q * SF_COLS_A, plain_desc(sf_base + (uint32_t)q * 512u), issue);
+#pragma unroll
+              for (int bb = 0; bb < SF_COLS_B / 4; ++bb)
+                tmem_cp_32x128b_warpx4<CG>(sfb_t + (uint32_t)q * SF_COLS_B + 4u * bb,
+                                           plain_desc(sf_base + (uint32_t)NSF * 512u * (1 + bb) + (uint32_t)q * 512u), issue);
+            }
+#pragma unroll
+            for (int ka = 0; ka < NA; ++ka) {
+              const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, RB);
+              const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, RB);
+#pragma unroll
+              for (int kk = 0; kk < KS; ++kk) {
+                const int q = ka * KS + kk;
+                mma_nvf4<CG>(d_tmem, ad + 2u * kk, bd + 2u * kk, idesc,
+                             sfa_t + (uint32_t)q * SF_COLS_A, sfb_t + (uint32_t)q * SF_COLS_B,
+                             (kb | ka | kk) != 0, issue);
               }
-              if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3); else mma_commit(empty_bar + 8u * stage);
             }
           } else {
-            if (mma_lane) {
-              for (int ka = 0; ka < n_atoms; ++ka) {
-                const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, row_b);
-                const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, row_b);
-                if (k_steps == 4) {   // 128-byte rows: the fully unrolled common case
 #pragma unroll
-                  for (int kk = 0; kk < 4; ++kk)
+            for (int ka = 0; ka < NA; ++ka) {
+              const uint64_t ad = swz_kmajor_desc(sbase + (uint32_t)ka * a_bytes, RB);
+              const uint64_t bd = swz_kmajor_desc(bbase + (uint32_t)ka * b_bytes, RB);
 #pragma unroll
-                    for (int h = 0; h < N_SUB; ++h)
-                      mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
-                                       bd + (uint64_t)((h * B_BOX * 128) >> 4) + 2u * kk, idesc, (kb | ka | kk) != 0);
-                } else {              // 64- or 32-byte rows (narrow TILE_K): 2 or 1 K steps
-                  for (int kk = 0; kk < k_steps; ++kk)
+              for (int kk = 0; kk < KS; ++kk)
 #pragma unroll
-                    for (int h = 0; h < N_SUB; ++h)
-                      mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
-                                       bd + (uint64_t)(((uint32_t)(h * B_BOX) * row_b) >> 4) + 2u * kk, idesc,
-                                       (kb | ka | kk) != 0);
-                }
-              }
-              if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3); else mma_commit(empty_bar + 8u * stage);
+                for (int h = 0; h < N_SUB; ++h)
+                  mma_ss<CG, KIND>(d_tmem + (uint32_t)(h * MMA_N), ad + 2u * kk,
+                                   bd + (uint64_t)(((uint32_t)(h * B_BOX) * RB) >> 4) + 2u * kk, idesc,
+                                   (kb | ka | kk) != 0, issue);
             }
           }
-          __syncwarp();
+          if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3, issue);
+          else mma_commit(empty_bar + 8u * stage, issue);
           TRACE_EVENT(2u, 2u, stage);
           issued = true;
           if (++stage == n_stages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        if (mma_lane) {
-          if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3); else mma_commit(tfull_bar + 8u * acc);
-        }
-        __syncwarp();
+        if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3, issue);
+        else mma_commit(tfull_bar + 8u * acc, issue);
         if (++acc == n_acc) { acc = 0; acc_phase ^= 1u; }
       }
       if (!ok && issued) {
         // Wait (bounded) until every MMA already issued has finished with TMEM.
-        if (mma_lane) {
-          if constexpr (CG == 2) mma_commit_pair(drain_bar, 0x1); else mma_commit(drain_bar);
-        }
-        __syncwarp();
+        if constexpr (CG == 2) mma_commit_pair(drain_bar, 0x1, issue);
+        else mma_commit(drain_bar, issue);
         drain_wait(drain_bar, 0, 100000000ull);
       }
-    }
+    });
   } else {
     // ------------------------------------------------------------ epilogue
     const uint32_t q = warp & 3u;                 // TMEM lane quadrant of this warp
@@ -652,6 +658,8 @@ int resolve(const GemmArgs* a, Resolved& r) {
            r.dt == 2 ? "" : ", or one or two MMA K steps");
     r.row_bytes = 128u;
     r.atoms = r.tile_k / ae;
+    if (r.atoms != 1 && r.atoms != 2 && r.atoms != 4)
+      FAIL("tile_k %d must be 1, 2 or 4 128-byte swizzle atoms (%d, %d or %d)", r.tile_k, ae, 2 * ae, 4 * ae);
   }
 
   // Element size in bytes (NVFP4: half a byte) and alignment (128-bit, as the reference's Alignment{A,B,D}).

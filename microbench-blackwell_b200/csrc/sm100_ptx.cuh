@@ -57,8 +57,13 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_bar) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+// Every issuing wrapper below takes a trailing predicate: a converged warp
+// executes the instruction with only the issuing lane's predicate set, so the
+// operands stay warp-uniform (no branch around the issue).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes, uint32_t pred = 1u) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+               "@q mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}"
+               :: "r"(bar), "r"(bytes), "r"(pred) : "memory");
 }
 // One non-blocking probe of phase `parity` (true once that phase completed).
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -142,42 +147,47 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
 }
 // 2-D tiled load into this CTA's shared memory, completing on `bar` (this CTA).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* m, uint32_t bar,
-                                            int32_t x, int32_t y, uint64_t policy) {
+                                            int32_t x, int32_t y, uint64_t policy, uint32_t pred = 1u) {
 #if !GEMM_TMA_CACHE_HINT
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];"
-      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y)
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+      "@q cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];\n\t}"
+      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "r"(pred)
       : "memory");
   return;
 #endif
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4}], [%2], %5;"
-      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "l"(policy)
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+      "@q cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;\n\t}"
+      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "l"(policy), "r"(pred)
       : "memory");
 }
 // 2-D tiled load into this CTA's shared memory whose completion is signalled
 // on the barrier `cluster_bar` of the pair's leader CTA (cta_group::2).
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, uint32_t cluster_bar,
-                                                 int32_t x, int32_t y, uint64_t policy) {
+                                                 int32_t x, int32_t y, uint64_t policy, uint32_t pred = 1u) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4}], [%2], %5;"
-      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(cluster_bar), "r"(x), "r"(y), "l"(policy)
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+      "@q cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;\n\t}"
+      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(cluster_bar), "r"(x), "r"(y), "l"(policy), "r"(pred)
       : "memory");
 }
 // Warm L2 with a 2-D tile (no shared-memory destination, no completion signal).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
-               :: "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y) : "memory");
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int32_t x, int32_t y, uint32_t pred = 1u) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t"
+               "@q cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];\n\t}"
+               :: "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(pred) : "memory");
 }
 // Plain bulk copy global -> shared (no tensor map); 16-byte aligned, size % 16 == 0.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
-                                          uint64_t policy) {
+                                          uint64_t policy, uint32_t pred = 1u) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-      :: "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+      "@q cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n\t}"
+      :: "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy), "r"(pred) : "memory");
 }
 
 // L2 cache policies (createpolicy): operands are re-read by other CTAs.
@@ -216,59 +226,63 @@ __device__ __forceinline__ void tc_fence_after() {
 // mbarrier protocol orders.
 template <int CG, int KIND>
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
+                                       uint32_t accumulate, uint32_t pred = 1u) {
   const uint32_t z = 0;
   if constexpr (CG == 1) {
     if constexpr (KIND == 0) {
       asm volatile(
-          "{\n\t.reg .pred p;\n\t"
-          "setp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-          :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z));
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+          "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+          :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(pred));
     } else {
       asm volatile(
-          "{\n\t.reg .pred p;\n\t"
-          "setp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-          :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z));
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+          "@q tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+          :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(pred));
     }
   } else {
     if constexpr (KIND == 0) {
       asm volatile(
-          "{\n\t.reg .pred p;\n\t"
-          "setp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
-          :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z));
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+          "@q tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+          :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(pred));
     } else {
       asm volatile(
-          "{\n\t.reg .pred p;\n\t"
-          "setp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
-          :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z));
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+          "@q tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+          :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(pred));
     }
   }
 }
 // Block-scaled NVFP4: e2m1 x e2m1 with ue4m3 scales per 16 K elements, scales in TMEM.
 template <int CG>
 __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate,
+                                         uint32_t pred = 1u) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::%7.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%4], [%5], p;\n\t}"
-      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate), "n"(CG)
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\tsetp.ne.b32 q, %8, 0;\n\t"
+      "@q tcgen05.mma.cta_group::%7.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%4], [%5], p;\n\t}"
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate), "n"(CG),
+         "r"(pred)
       : "memory");
 }
 
 // Arrive on `bar` (this CTA) once every prior tcgen05 op of this thread completes.
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-               :: "r"(bar) : "memory");
+__device__ __forceinline__ void mma_commit(uint32_t bar, uint32_t pred = 1u) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+               "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+               :: "r"(bar), "r"(pred) : "memory");
 }
 // Pair form: arrive on the barrier at offset `bar` in every CTA of `cta_mask`.
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
-               :: "r"(bar), "h"(cta_mask) : "memory");
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask, uint32_t pred = 1u) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+               "@q tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}"
+               :: "r"(bar), "h"(cta_mask), "r"(pred) : "memory");
 }
 
 // 32 lanes x 32 bits, 32 consecutive columns per thread.
@@ -299,8 +313,10 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // Shared -> TMEM copy of scale factors: 32 rows x 128 bits replicated to the
 // four 32-lane quadrants of TMEM (the scale-factor layout the block-scaled MMA reads).
 template <int CG>
-__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::%2.32x128b.warpx4 [%0], %1;" :: "r"(taddr), "l"(sdesc), "n"(CG) : "memory");
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc, uint32_t pred = 1u) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t"
+               "@q tcgen05.cp.cta_group::%2.32x128b.warpx4 [%0], %1;\n\t}"
+               :: "r"(taddr), "l"(sdesc), "n"(CG), "r"(pred) : "memory");
 }
 
 // ------------------------------------------------------------------ descriptors
