@@ -105,6 +105,7 @@ struct KernelParams {
   const uint8_t* sfa;
   const uint8_t* sfb;
   int32_t sf_kblocks;     // K / 64 (NVFP4 scale atoms along K)
+  int32_t sf_slots;       // NVFP4: TMEM scale-factor slots (stage s uses slot s % sf_slots)
   int32_t l2_prefetch;    // k-blocks the L2 prefetch cursor runs ahead of the loads (0 = off)
   int32_t num_acc;        // accumulator buffers in TMEM (2 = epilogue overlaps the next tile)
 };
@@ -220,12 +221,13 @@ template <int DT, int CG, int BN>
 __global__ void __launch_bounds__(threads_for(BN), 1)
 gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
+                   const __grid_constant__ CUtensorMap tmap_sfa,   // NVFP4 pair kernel only
+                   const __grid_constant__ CUtensorMap tmap_sfb,   // NVFP4 pair kernel only
                    const __grid_constant__ KernelParams p) {
   // A rows per CTA.  128 fills the 128 TMEM lanes; a 1-SM TILE_M = 64 tile
   // (M = 64 MMA) puts row r of the accumulator in lane 32*(r/16) + r%16, i.e.
   // the first 16 lanes of each 32-lane quadrant.
   const int BM = CG == 2 ? 128 : p.cta_rows;
-  constexpr int BN_CTA = BN / CG;         // B rows per CTA
   constexpr int MMA_N = BN > 256 ? 256 : BN;  // N of one tcgen05.mma
   constexpr int N_SUB = BN / MMA_N;       // MMAs per K step (N halves of a 512-wide pair tile)
   constexpr int B_BOX = MMA_N / CG;       // B rows per CTA per N half (one TMA box)
@@ -261,6 +263,10 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
+    if constexpr (DT == 2 && CG == 2) {
+      prefetch_tmap(&tmap_sfa);
+      prefetch_tmap(&tmap_sfb);
+    }
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(full_bar + 8u * s, 1);
       mbar_init(empty_bar + 8u * s, 1);
@@ -383,18 +389,27 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           }
           if constexpr (DT == 2) {
             // Scale factors: one 512-byte atom (128 rows x 4 scales) per 64 K
-            // elements; a stage covers NA*4 of them for A, and for B
-            // ceil(BN_CTA/128) row blocks each.
+            // elements; a stage covers NA*4 of them for this CTA's 128 rows of
+            // A, and for each of the tile's BN/128 row blocks of B (the whole
+            // tile N, also in a CTA pair, whose MMA reads every B scale from
+            // each CTA's own TMEM).
             const uint32_t sf_base = sbase + (uint32_t)NA * (a_bytes + b_bytes);
             const int kq0 = kb * NA * 4;
             constexpr int NSF = NA * 4;
-            const uint8_t* sfa_src = p.sfa + ((int64_t)(m0 / 128) * p.sf_kblocks + kq0) * 512;
-            bulk_load(sf_base, sfa_src, (uint32_t)NSF * 512u, target, policy, issue);
-            constexpr int B_BLOCKS = (BN_CTA + 127) / 128;
+            if constexpr (CG == 2) {
+              // 3-D maps (512-byte atom, K atom, row block): the loads signal
+              // the leader's barrier like the pair's A/B loads.
+              tma_load_3d_pair(sf_base, &tmap_sfa, target, 0, kq0, m0 / 128, policy, issue);
+              tma_load_3d_pair(sf_base + (uint32_t)NSF * 512u, &tmap_sfb, target, 0, kq0, un * (BN / 128), policy,
+                               issue);
+            } else {
+              const uint8_t* sfa_src = p.sfa + ((int64_t)(m0 / 128) * p.sf_kblocks + kq0) * 512;
+              bulk_load(sf_base, sfa_src, (uint32_t)NSF * 512u, target, policy, issue);
 #pragma unroll
-            for (int bb = 0; bb < B_BLOCKS; ++bb) {
-              const uint8_t* sfb_src = p.sfb + ((int64_t)(n0 / 128 + bb) * p.sf_kblocks + kq0) * 512;
-              bulk_load(sf_base + (uint32_t)NSF * 512u * (1 + bb), sfb_src, (uint32_t)NSF * 512u, target, policy, issue);
+              for (int bb = 0; bb < BN / 128; ++bb) {
+                const uint8_t* sfb_src = p.sfb + ((int64_t)(n0 / 128 + bb) * p.sf_kblocks + kq0) * 512;
+                bulk_load(sf_base + (uint32_t)NSF * 512u * (1 + bb), sfb_src, (uint32_t)NSF * 512u, target, policy, issue);
+              }
             }
           }
           TRACE_EVENT(1u, 2u, stage);
@@ -435,13 +450,21 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const uint32_t st_bytes = p.stage_bytes, a_bytes = p.a_atom_bytes, b_bytes = p.b_atom_bytes;
       const uint32_t idesc = p.idesc;
       const int n_acc = p.num_acc;
+      // NVFP4: each stage's scales go to the next of p.sf_slots TMEM slots, so
+      // the copy for stage s+1 never overwrites scales the MMAs of stage s are
+      // still reading (one shared slot would drain the tensor pipe per stage).
+      const int n_sf_slots = DT == 2 ? p.sf_slots : 1;
+      int sf_slot = 0;
+      (void)n_sf_slots;
+      (void)sf_slot;
       for (int u = pair; u < n_units && ok; u += num_pairs) {
         const bool wt = wait_bar<CG == 2>(tempty_bar + 8u * acc, acc_phase ^ 1u, ctl, ROLE_MMA, 0x80u | acc);
         if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ready = false;   // next stage's data already seen (probed after the previous commit)
         for (int kb = 0; kb < n_kb; ++kb) {
-          const bool w = wait_bar<CG == 2>(full_bar + 8u * stage, phase, ctl, ROLE_MMA, stage);
+          const bool w = ready || wait_bar<CG == 2>(full_bar + 8u * stage, phase, ctl, ROLE_MMA, stage);
           if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
           TRACE_EVENT(2u, 1u, stage);
           tc_fence_after();
@@ -452,8 +475,10 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
             // accumulators), then issue the block-scaled MMAs.
             const uint32_t sf_base = bbase + (uint32_t)NA * b_bytes;
             constexpr int NSF = NA * 4;
-            const uint32_t sfa_t = tmem_base + (uint32_t)(n_acc * BN);
+            constexpr uint32_t SF_STAGE_COLS = (uint32_t)NSF * (SF_COLS_A + SF_COLS_B);
+            const uint32_t sfa_t = tmem_base + (uint32_t)(n_acc * BN) + (uint32_t)sf_slot * SF_STAGE_COLS;
             const uint32_t sfb_t = sfa_t + (uint32_t)NSF * SF_COLS_A;
+            if (++sf_slot == n_sf_slots) sf_slot = 0;
 #pragma unroll
             for (int q = 0; q < NSF; ++q) {
               tmem_cp_32x128b_warpx4<CG>(sfa_t + (uint32_t)q * SF_COLS_A, plain_desc(sf_base + (uint32_t)q * 512u), issue);
@@ -493,6 +518,10 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           TRACE_EVENT(2u, 2u, stage);
           issued = true;
           if (++stage == n_stages) { stage = 0; phase ^= 1u; }
+          // Probe the next stage now so the barrier round trip overlaps the
+          // MMAs just issued instead of opening the next iteration.
+          ready = CG == 2 ? mbar_test_wait_cluster(full_bar + 8u * stage, phase)
+                          : mbar_test_wait(full_bar + 8u * stage, phase);
         }
         if (!ok) break;
         if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3, issue);
@@ -597,7 +626,7 @@ struct Resolved {
   int dt, cg, bm, bn, tile_k, atoms, stages, max_stages, cluster_m;
   uint32_t a_atom_bytes, b_atom_bytes, sf_stage_bytes, stage_bytes;
   int64_t smem_bytes;
-  int tmem_cols, num_acc, threads;
+  int tmem_cols, num_acc, threads, sf_slots;
   uint32_t row_bytes;
   int num_m_units, num_n_units, num_units, num_k_blocks;
   int grid, num_sms, raster_group;
@@ -671,10 +700,9 @@ int resolve(const GemmArgs* a, Resolved& r) {
   if (((uintptr_t)a->a | (uintptr_t)a->b | (uintptr_t)a->d) & 15) FAIL("A/B/D must be 16-byte aligned");
   if ((a->k * bits) % 128 != 0) FAIL("k must be a multiple of %lld", (long long)(128 / bits));
   if (r.dt == 2) {
-    if (r.cg != 1) FAIL("NVFP4 is implemented for cta_group 1 only");
     if (a->k % r.tile_k != 0) FAIL("NVFP4 needs k %% tile_k == 0");
-    if (a->m % 128 != 0 || a->n % r.bn != 0) FAIL("NVFP4 needs m %% 128 == 0 and n %% tile_n == 0");
-    if (r.bn % 128 != 0) FAIL("NVFP4 needs tile_n 128 or 256 (scale atoms are 128 rows)");
+    if (a->m % r.bm != 0 || a->n % r.bn != 0) FAIL("NVFP4 needs m %% %d == 0 and n %% tile_n == 0", r.bm);
+    if (r.bn != 128 && r.bn != 256) FAIL("NVFP4 needs tile_n 128 or 256 (scale atoms are 128 rows)");
     if (((uintptr_t)a->sfa | (uintptr_t)a->sfb) & 15) FAIL("sfa/sfb must be 16-byte aligned");
   }
 
@@ -682,7 +710,7 @@ int resolve(const GemmArgs* a, Resolved& r) {
   r.b_atom_bytes = (uint32_t)(r.bn / r.cg) * r.row_bytes;
   r.sf_stage_bytes = 0;
   if (r.dt == 2) {
-    const int b_blocks = (r.bn / r.cg + 127) / 128;
+    const int b_blocks = r.bn / 128;   // every CTA (also of a pair) stages the whole tile's B scales
     r.sf_stage_bytes = (uint32_t)(r.atoms * 4 * 512 * (1 + b_blocks));
   }
   r.stage_bytes = (uint32_t)r.atoms * (r.a_atom_bytes + r.b_atom_bytes) + r.sf_stage_bytes;
@@ -698,15 +726,23 @@ int resolve(const GemmArgs* a, Resolved& r) {
   // CTA would only stall in tcgen05.alloc until the first frees its columns.
   if (r.smem_bytes < kMinSmemPerCta) r.smem_bytes = kMinSmemPerCta;
 
-  int sf_cols = 0;
+  int sf_cols = 0;   // TMEM columns of one stage's scale factors
   if (r.dt == 2) {
     const int nsf = r.atoms * 4;
     sf_cols = nsf * 4 + nsf * ((r.bn + 127) / 128) * 4;
   }
   // Two accumulator buffers when they fit (the epilogue then overlaps the
-  // next tile's mainloop), else one.
+  // next tile's mainloop), else one.  NVFP4 scale factors then take as many
+  // per-stage slots (up to 4, at most the stage count) as the columns left allow.
   r.num_acc = 2 * r.bn + sf_cols <= 512 ? 2 : 1;
-  const int cols = r.num_acc * r.bn + sf_cols;
+  r.sf_slots = 1;
+  if (sf_cols > 0) {
+    r.sf_slots = (512 - r.num_acc * r.bn) / sf_cols;
+    if (r.sf_slots > 4) r.sf_slots = 4;
+    if (r.sf_slots > r.stages) r.sf_slots = r.stages;
+    if (r.sf_slots < 1) r.sf_slots = 1;
+  }
+  const int cols = r.num_acc * r.bn + r.sf_slots * sf_cols;
   if (cols > 512) FAIL("TMEM: %d columns needed (accumulator + scales) > 512", cols);
   r.tmem_cols = next_pow2_cols(cols);
   r.threads = threads_for(r.bn);
@@ -747,7 +783,21 @@ bool encode_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType t, uint64_t 
   return res == CUDA_SUCCESS;
 }
 
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, KernelParams);
+// Scale-factor tensor map: dims (128 x uint32 = one 512-byte atom, K/64 atoms,
+// row blocks of 128), no swizzle; box (128, nsf atoms, row blocks).
+bool encode_sf_3d(CUtensorMap* m, const void* ptr, uint64_t kblocks, uint64_t row_blocks, uint32_t box_kb,
+                  uint32_t box_rb) {
+  cuuint64_t dims[3] = {128, kblocks, row_blocks};
+  cuuint64_t strides[2] = {512, kblocks * 512};
+  cuuint32_t box[3] = {128, box_kb, box_rb};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult res = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return res == CUDA_SUCCESS;
+}
+
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, KernelParams);
 
 template <int DT, int CG, int BN>
 KernelFn kernel_ptr() { return gemm_sm100a_kernel<DT, CG, BN>; }
@@ -829,6 +879,19 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
                  (uint32_t)((r.bn > 256 ? 256 : r.bn) / r.cg), r.row_bytes))
     return GEMM_ERR_CANNOT_IMPLEMENT;
 
+  // NVFP4 pair kernel: scale factors through 3-D maps (uint32 x 128 = one
+  // 512-byte atom, K/64 atoms per row block, row blocks), one stage's atoms
+  // per box: SFA one row block, SFB the tile's BN/128 row blocks.
+  CUtensorMap tm_sfa, tm_sfb;
+  memset(&tm_sfa, 0, sizeof(tm_sfa));
+  memset(&tm_sfb, 0, sizeof(tm_sfb));
+  if (r.dt == 2 && r.cg == 2) {
+    const uint32_t nsf = (uint32_t)r.atoms * 4u;
+    if (!encode_sf_3d(&tm_sfa, a.sfa, (uint64_t)(a.k / 64), (uint64_t)(a.m / 128), nsf, 1u) ||
+        !encode_sf_3d(&tm_sfb, a.sfb, (uint64_t)(a.k / 64), (uint64_t)(a.n / 128), nsf, (uint32_t)(r.bn / 128)))
+      return GEMM_ERR_CANNOT_IMPLEMENT;
+  }
+
   KernelParams p;
   memset(&p, 0, sizeof(p));
   p.m = (int32_t)a.m; p.n = (int32_t)a.n; p.k = (int32_t)a.k;
@@ -850,6 +913,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   p.sfa = reinterpret_cast<const uint8_t*>(a.sfa);
   p.sfb = reinterpret_cast<const uint8_t*>(a.sfb);
   p.sf_kblocks = (int32_t)(a.k / 64);
+  p.sf_slots = r.sf_slots;
   p.l2_prefetch = a.l2_prefetch < 0 ? 0 : (a.l2_prefetch == 0 ? kDefaultL2Prefetch : a.l2_prefetch);
 
   KernelFn fn = pick_kernel(r.dt, r.cg, r.bn);
@@ -872,7 +936,7 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tma_a, tmb_b, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tma_a, tmb_b, tm_sfa, tm_sfb, p);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return GEMM_ERR_LAUNCH;

@@ -175,6 +175,20 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(cluster_bar), "r"(x), "r"(y), "l"(policy), "r"(pred)
       : "memory");
 }
+// 3-D tiled load into this CTA's shared memory whose completion is signalled
+// on the pair leader's barrier `cluster_bar` (cta_group::2); used for the
+// NVFP4 scale-factor atoms of the pair kernel.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* m, uint32_t cluster_bar,
+                                                 int32_t x, int32_t y, int32_t z, uint64_t policy,
+                                                 uint32_t pred = 1u) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %7, 0;\n\t"
+      "@q cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;\n\t}"
+      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z), "l"(policy),
+         "r"(pred)
+      : "memory");
+}
 // Warm L2 with a 2-D tile (no shared-memory destination, no completion signal).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int32_t x, int32_t y, uint32_t pred = 1u) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t"

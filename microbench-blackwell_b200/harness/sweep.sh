@@ -40,7 +40,7 @@ else
   BF16_TILES=("128,128,64" "128,192,64" "128,256,64" "128,256,128")
   FP8_TILES=("128,128,128" "128,192,128" "128,256,128" "128,256,256")
 fi
-NVFP4_TILES=("128,128,256" "128,192,256" "128,256,256")
+NVFP4_TILES=("128,128,256" "128,256,256" "256,128,256" "256,256,256")
 PAIR_BF16_TILES=("256,256,64" "256,512,64" "256,256,128")
 PAIR_FP8_TILES=("256,256,128" "256,512,128" "256,256,256")
 

@@ -122,6 +122,20 @@ def test_tile_m_64_is_a_1sm_tile(pkg, dtype, tile_k):
     assert rc == pkg.ERR_CANNOT_IMPLEMENT and b"tile_m" in info.reason
 
 
+def test_nvfp4_pair_query(pkg):
+    """NVFP4 cta_group::2: 256 x tile_n tiles; each CTA stages its 128 rows of
+    A scales and the whole tile's B scales; one accumulator at tile_n 256."""
+    args = _args(pkg, dtype=pkg.NVFP4, cta_group=2, tile_n=256, tile_k=256, sfa=0x40000, sfb=0x50000)
+    rc, info = pkg.query(args)
+    assert rc == pkg.OK, info.reason
+    assert info.tile_m == 256 and info.cta_group == 2
+    # per CTA: A 128 rows + B 128 rows of 128 B, SFA 4 atoms, SFB 4 atoms x 2 row blocks
+    assert info.smem_bytes_per_stage == (128 + 128) * 128 + 4 * 512 * (1 + 2)
+    rc, info = pkg.query(_args(pkg, dtype=pkg.NVFP4, cta_group=2, tile_n=256, tile_k=256, m=8192 - 128,
+                               sfa=0x40000, sfb=0x50000))
+    assert rc == pkg.ERR_CANNOT_IMPLEMENT and b"m %" in info.reason
+
+
 def test_null_pointers_are_bad_args(pkg):
     rc, _ = pkg.query(_args(pkg, a=None))
     assert rc == pkg.ERR_BAD_ARGS

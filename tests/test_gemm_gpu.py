@@ -316,6 +316,46 @@ def test_nvfp4_matches_oracle(pkg, orc, cuda, m, n, k, tile_n, stages):
     assert err <= TOL[2], err
 
 
+# --------------------------------------------------------------------------- NVFP4 (CTA pair)
+@pytest.mark.parametrize("tile_n", [128, 256])
+def test_nvfp4_pair_identity_b_pins_sfa_on_both_ctas(pkg, orc, cuda, tile_n):
+    """cta_group::2 block-scaled MMA: D = A . I^T reproduces A exactly, so the
+    scale factors of A reach the TMEM of both CTAs of the pair in place."""
+    m, n, k = 512, 256, 512
+    ops = pkg.make_operands(pkg.NVFP4, m, n, k, seed=4, device=cuda)
+    ops.b.copy_(nvfp4_identity(cuda, n, k))
+    ops.sfb.fill_(UE4M3_ONE)
+    pkg.gemm(ops, cta_group=2, tile_n=tile_n, tile_k=256)
+    A = orc.dequant_nvfp4(ops.a.cpu().numpy(), ops.sfa.cpu().numpy(), k)
+    D = orc.bf16_bits_to_f32(raw_u16(ops.d.t().contiguous()))
+    np.testing.assert_array_equal(D, A[:, :n])
+
+
+@pytest.mark.parametrize("tile_n", [128, 256])
+def test_nvfp4_pair_identity_a_pins_sfb(pkg, orc, cuda, tile_n):
+    """The mirror case: every CTA of the pair stages the whole tile's B scales."""
+    m, n, k = 256, 512, 512
+    ops = pkg.make_operands(pkg.NVFP4, m, n, k, seed=5, device=cuda)
+    ops.a.copy_(nvfp4_identity(cuda, m, k))
+    ops.sfa.fill_(UE4M3_ONE)
+    pkg.gemm(ops, cta_group=2, tile_n=tile_n, tile_k=256)
+    B = orc.dequant_nvfp4(ops.b.cpu().numpy(), ops.sfb.cpu().numpy(), k)
+    D = orc.bf16_bits_to_f32(raw_u16(ops.d.t().contiguous()))
+    np.testing.assert_array_equal(D, B[:, :m].T)
+
+
+@pytest.mark.parametrize("m,n,k,tile_n,tile_k,stages", [(512, 512, 2048, 256, 256, 0), (256, 384, 1024, 128, 256, 0),
+                                                        (768, 1024, 4096, 256, 512, 0), (512, 256, 1024, 256, 256, 2)])
+def test_nvfp4_pair_matches_oracle_and_single_sm_bitwise(pkg, orc, cuda, m, n, k, tile_n, tile_k, stages):
+    ops = pkg.make_operands(pkg.NVFP4, m, n, k, seed=1, device=cuda)
+    pkg.gemm(ops, cta_group=2, tile_n=tile_n, tile_k=tile_k, stages=stages)
+    assert rel_err(orc, pkg, ops) <= TOL[2]
+    pair = ops.d.clone()
+    ops.d.fill_(0)
+    pkg.gemm(ops, cta_group=1, tile_n=tile_n, tile_k=tile_k)
+    assert torch.equal(ops.d, pair)
+
+
 def test_config4_nvfp4_mlp_sampled(pkg, orc, cuda):
     """NVFP4 M=8192, N=28672, K=8192; sampled fp64 check."""
     m, n, k = 8192, 28672, 8192
