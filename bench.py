@@ -49,7 +49,7 @@ WORKLOADS = {
                            knobs=dict(tile_n=512, tile_k=128, stages=0, cta_group=2, raster_group=16),
                            a=("normal", 0.25), b=("normal", 0.25), config=3),
     "nvfp4_mlp": dict(dtype="nvfp4", m=8192, n=28672, k=8192,
-                      knobs=dict(tile_n=256, tile_k=256, stages=0, cta_group=1, raster_group=16),
+                      knobs=dict(tile_n=256, tile_k=256, stages=0, cta_group=1, raster_group=-16),
                       a=("normal", 1.0), b=("normal", 1.0), config=4),
     "e4m3_nsplit": dict(dtype="e4m3", m=16384, n=57344, k=8192,
                         knobs=dict(tile_n=512, tile_k=128, stages=0, cta_group=2, raster_group=16),
