@@ -466,9 +466,15 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
                           sfb=None if ops.sfb is None else ops.sfb.data_ptr(), **wl["knobs"])
         L = pkg.lib()
         sp = C.c_void_p(stream.cuda_stream)
-        for _ in range(3):
-            L.gemm_sm100a_launch(C.byref(g), sp)
-        stream.synchronize()
+        # Untimed settle (>= 3 launches, ~0.25 s): the clock reaches this configuration's
+        # own power-capped steady state instead of the previous configuration's.
+        settle_end = time.perf_counter() + 0.25
+        n_settle = 0
+        while n_settle < 3 or time.perf_counter() < settle_end:
+            for _ in range(4):
+                L.gemm_sm100a_launch(C.byref(g), sp)
+            n_settle += 4
+            stream.synchronize()
         if world > 1:
             dist.barrier(device_ids=[local_rank])
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
