@@ -460,6 +460,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       for (int u = pair; u < n_units && ok; u += num_pairs) {
         const bool wt = wait_bar<CG == 2>(tempty_bar + 8u * acc, acc_phase ^ 1u, ctl, ROLE_MMA, 0x80u | acc);
         if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
+        TRACE_EVENT(2u, 3u, acc);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ready = false;   // next stage's data already seen (probed after the previous commit)
@@ -526,6 +527,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (!ok) break;
         if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3, issue);
         else mma_commit(tfull_bar + 8u * acc, issue);
+        TRACE_EVENT(2u, 4u, acc);
         if (++acc == n_acc) { acc = 0; acc_phase ^= 1u; }
       }
       if (!ok && issued) {
@@ -543,6 +545,8 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t leader_tempty = CG == 2 ? mapa_shared(tempty_bar, 0) : tempty_bar;
+    unsigned trace_i = 0;
+    (void)trace_i;
     for (int u = pair; u < p.num_units; u += num_pairs) {
       int um, un;
       unit_coords(u, p, um, un);
@@ -550,6 +554,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       // lane must agree to proceed even if one lane saw an abort.
       const bool ok = wait_bar<false>(tfull_bar + 8u * acc, acc_phase, ctl, ROLE_EPILOGUE, acc);
       if (!__all_sync(0xffffffffu, ok)) break;
+      if (warp == 2) TRACE_EVENT(3u, 1u, acc);
       tc_fence_after();
       const int q_rows = BM / 4;                  // accumulator rows in this warp's quadrant
       const int64_t row = (int64_t)um * MMA_M + (int64_t)cta_rank * BM + q_rows * (int)q + lane;
@@ -557,17 +562,55 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const bool row_ok = (int)lane < q_rows && row < p.m;
       __nv_bfloat16* const dptr = p.d + row;
       const uint32_t t_row = tmem_base + ((32u * q) << 16) + (uint32_t)(acc * BN);
+      bool released = false;
       if constexpr (COLS % 32 == 0) {
-#pragma unroll 1
-        for (int c = c_begin; c < c_begin + COLS; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(t_row + (uint32_t)c, r);
-          tmem_ld_wait();
-          if (row_ok) {
+        if (p.num_acc == 1) {
+          // Single accumulator (the tile fills TMEM): drain it into registers
+          // as packed bf16 pairs, release it at once so the next tile's MMAs
+          // start, then write D while that mainloop runs.
+          uint32_t pk[COLS / 2];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int64_t col = n0 + c + j;
-              if (col < p.n) dptr[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+          for (int cc = 0; cc < COLS; cc += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + (uint32_t)(c_begin + cc), r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(p.alpha * __uint_as_float(r[j]),
+                                                             p.alpha * __uint_as_float(r[j + 1]));
+              pk[(cc + j) / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 2) mbar_arrive_cluster(leader_tempty + 8u * acc); else mbar_arrive(tempty_bar + 8u * acc);
+          }
+          released = true;
+          if (row_ok) {
+            const int64_t col0 = n0 + c_begin;
+            const int64_t left = (int64_t)p.n - col0;
+            const int n_valid = left < (int64_t)COLS ? (int)left : COLS;   // columns inside D
+            uint16_t* dst = reinterpret_cast<uint16_t*>(dptr) + col0 * p.ldd;
+            const int64_t step = p.ldd;
+#pragma unroll
+            for (int j = 0; j < COLS; ++j) {
+              if (j < n_valid) *dst = (uint16_t)(j % 2 == 0 ? (pk[j / 2] & 0xFFFFu) : (pk[j / 2] >> 16));
+              dst += step;
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = c_begin; c < c_begin + COLS; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + (uint32_t)c, r);
+            tmem_ld_wait();
+            if (row_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int64_t col = n0 + c + j;
+                if (col < p.n) dptr[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+              }
             }
           }
         }
@@ -586,11 +629,14 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if constexpr (CG == 2) mbar_arrive_cluster(leader_tempty + 8u * acc); else mbar_arrive(tempty_bar + 8u * acc);
+      if (!released) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 2) mbar_arrive_cluster(leader_tempty + 8u * acc); else mbar_arrive(tempty_bar + 8u * acc);
+        }
       }
+      if (warp == 2) TRACE_EVENT(3u, 2u, acc);
       if (++acc == p.num_acc) { acc = 0; acc_phase ^= 1u; }
     }
   }
