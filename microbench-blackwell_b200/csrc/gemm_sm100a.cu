@@ -9,16 +9,22 @@
 // 1-SM (cta_group::1, 128 x BN) and 2-SM (cta_group::2, 256 x BN per CTA pair)
 // forms.
 //
-// One CTA of 192 threads per SM (persistent over output tiles):
+// One CTA per SM (persistent over output tiles), 192 threads (320 when the
+// tile fills TMEM):
 //   warp 0      TMA producer: 128B-swizzled A/B k-atoms into a STAGES-deep
 //               shared-memory ring, guarded by full/empty mbarriers (a TILE_K
 //               narrower than 128 bytes is one 64B- or 32B-swizzled atom).
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer; commits
-//               free ring slots and hands finished accumulators to the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (32 lanes each),
-//               alpha scale, bf16 round, coalesced column-major stores.
-// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
-// of tile i overlaps the mainloop of tile i+1.
+//   warp 1      TMEM allocator + tcgen05.mma issuer; commits free ring slots
+//               and hands finished accumulators to the epilogue.
+//   warps 2..   epilogue (4, or 8): tcgen05.ld of the fp32 accumulator (one
+//               TMEM lane quadrant each), alpha scale, bf16 round, column-major
+//               stores.
+// Warps 0 and 1 run their loops converged, so addresses and descriptors are
+// warp-uniform, with every TMA / mbarrier / tcgen05 issue predicated on one
+// elected lane; the loops are instantiated per stage shape (atoms x MMA K
+// steps).  The accumulator is double-buffered in TMEM (2 x BN columns) when it
+// fits, so the epilogue of tile i overlaps the mainloop of tile i+1; a single
+// accumulator is drained into registers and released before D is written.
 //
 // Every mbarrier wait is bounded (globaltimer budget): on expiry the kernel
 // records a status word, tells the other roles to stop, drains its own
