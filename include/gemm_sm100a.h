@@ -65,8 +65,8 @@ enum {
  * (cutlass_gemm_bench.cu:34-49: TILE_M=128, TILE_N=128, TILE_K=64,
  * STAGES=0 meaning "auto", DTYPE_ID=0); here they are runtime fields.
  * cta_group (1 or 2) selects 1-SM or 2-SM (CTA pair) MMAs; cluster_m is the
- * number of CTAs per cluster along M (equal to cta_group, or 2*cta_group for
- * B-operand multicast on one GPU).
+ * number of CTAs per cluster along M and must equal cta_group (no load uses
+ * cluster multicast).
  *
  * Leading dimensions are in ELEMENTS (for NVFP4, elements are 4-bit; lda and
  * ldb must then be even).  All base pointers must be 16-byte aligned and
@@ -77,7 +77,9 @@ enum {
  * 128-row x 4-scale interleaved atom layout: for row r and scale column c
  * (c = k / 16) the byte offset is
  *     ((r / 128) * (K / 64) + c / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (c % 4)
- * M (and N) are padded up to a multiple of 128 rows in this layout.
+ * NVFP4 needs m a multiple of the MMA M (128, or 256 for cta_group 2), n a
+ * multiple of tile_n and k a multiple of tile_k; the scale buffers then hold
+ * (m / 128) * (k / 64) and (n / 128) * (k / 64) atoms of 512 bytes.
  */
 typedef struct GemmArgs {
   uint32_t struct_size;   /* sizeof(GemmArgs), guards ABI drift */
@@ -89,9 +91,12 @@ typedef struct GemmArgs {
   const void* sfa;        /* NVFP4 only */
   const void* sfb;        /* NVFP4 only */
   float    alpha;         /* D = alpha * acc; 1.0 in the reference */
-  int32_t  tile_m;        /* per-MMA M: 128 (cta_group 1) or 256 (cta_group 2); 0 = default */
-  int32_t  tile_n;        /* 16..256, multiple of 16; 0 = default (256) */
-  int32_t  tile_k;        /* K per pipeline stage, multiple of the 128-byte swizzle span; 0 = default */
+  int32_t  tile_m;        /* per-MMA M: 64 or 128 (cta_group 1), 256 (cta_group 2); 0 = default */
+  int32_t  tile_n;        /* cta_group 1: 16, 32, 64, 128, 192, 256; cta_group 2: 64, 128, 192, 256, 512;
+                             NVFP4: 128 or 256; 0 = default (256) */
+  int32_t  tile_k;        /* K per pipeline stage: one or two 32-byte MMA K steps (bf16 16/32, fp8 32/64),
+                             or 1, 2 or 4 128-byte swizzle atoms (bf16 64/128/256, fp8 128/256/512,
+                             NVFP4 256/512/1024); 0 = one atom */
   int32_t  stages;        /* shared-memory ring depth; 0 = auto (as many as fit) */
   int32_t  cta_group;     /* 1 or 2; 0 = default (1) */
   int32_t  cluster_m;     /* CTAs per cluster along M; 0 = cta_group */
