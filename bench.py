@@ -366,6 +366,9 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
                      "GBps_per_rank": recv / (ag_ms * 1e-3) / 1e9, "collective": "ncclAllGather (torch.distributed)"}
         del full
 
+    # ---------------------------------------------------------- the reference's kernel family, same box
+    ref_full = run_reference_cutlass_full(pkg, ops, gargs, stream, wl["dtype"], args.steps)
+
     # ---------------------------------------------------------- end to end (host buffers)
     e2e = run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank)
 
@@ -414,6 +417,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
         "gpu_launches": args.steps,
         "cpu_baseline": cpu,
         "single_cta": single,
+        "reference_cutlass_full": ref_full,
         "allgather": allgather,
         "per_dtype": per_dtype,
         "kernel": {"grid": info.grid_ctas, "stages": info.stages, "tile": [info.tile_m, info.tile_n, info.tile_k],
@@ -487,12 +491,14 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
         flop_total = pkg.flops(m, n, k) * world
         tf = flop_total / (ms * 1e-3) / 1e12
         per_gpu = tf / world
+        ref_full = run_reference_cutlass_full(pkg, ops, g, stream, wl["dtype"], steps)
         peak = measured_umma_peak(pkg, wl["dtype"], dev)
         out[label] = {"workload": name, "baseline_config": wl["config"], "scaling": scaling,
                       "m": m, "n_total": n * world, "k": k, "knobs": wl["knobs"], "steps": steps,
                       "ms_per_step": ms, "tflops": tf, "tflops_per_gpu": per_gpu,
                       "umma_peak_tflops": peak["tflops"], "umma_peak_sm_mhz": peak["sm_mhz"],
-                      "pct_measured_umma_peak": 100.0 * per_gpu / peak["tflops"]}
+                      "pct_measured_umma_peak": 100.0 * per_gpu / peak["tflops"],
+                      "reference_cutlass_full": ref_full}
         del ops
         torch.cuda.empty_cache()
     return out
@@ -605,6 +611,65 @@ def run_single_cta(pkg, wl, dev, stream):
     out["ratio_vs_published"] = out["tflops"] / REF_SINGLE_CTA_TFLOPS[wl["dtype"]]
     out["binary"] = binp.name
     return out
+
+
+CUTLASS_REF_KERNEL = {"bf16": "CUTLASS SM100 1SM 128x256x64, 4 stages (cutlass_gemm_mainloop/results.csv:461)",
+                      "e4m3": "CUTLASS SM100 1SM 128x256x128, auto stages (cutlass_gemm_mainloop/results.csv:938)"}
+
+
+def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
+    """The reference's own CUTLASS kernel family at its best tile (oracle/_ref/libcutlass_ref.so,
+    the cutlass_gemm_bench.cu:101-156 type chain) on the same operands over the whole GPU,
+    timed interleaved with ours (2 rounds each) so both see the same clock state.
+    Informational: the reference itself only runs one CTA."""
+    import torch
+    code = {"bf16": 0, "e4m3": 1}.get(dtype)
+    lib = ROOT / "oracle" / "_ref" / "libcutlass_ref.so"
+    if code is None:
+        return None
+    if not lib.exists():
+        return {"unavailable": "oracle/_ref/libcutlass_ref.so not built (oracle/ref_build.sh needs the reference tree)"}
+    R = C.CDLL(str(lib))
+    R.cutlass_ref_gemm.restype = C.c_int
+    R.cutlass_ref_gemm.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                   C.c_int, C.c_void_p]
+    L = pkg.lib()
+    sp = C.c_void_p(stream.cuda_stream)
+    d_ref = torch.empty_like(ops.d)
+
+    def cut():
+        return R.cutlass_ref_gemm(code, ops.a.data_ptr(), ops.b.data_ptr(), d_ref.data_ptr(),
+                                  ops.m, ops.n, ops.k, 0, sp)
+
+    def ours():
+        return L.gemm_sm100a_launch(C.byref(gargs), sp)
+
+    def timed(fn, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            if fn() != 0:
+                return None
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    for _ in range(3):
+        if cut() != 0:
+            return {"unavailable": "cutlass_ref_gemm cannot run this problem"}
+        ours()
+    stream.synchronize()
+    n = max(5, min(steps, 50))
+    t_cut, t_ours = [], []
+    for _ in range(2):
+        t_ours.append(timed(ours, n))
+        t_cut.append(timed(cut, n))
+    if None in t_cut or None in t_ours:
+        return {"unavailable": "launch failed"}
+    flop = pkg.flops(ops.m, ops.n, ops.k)
+    return {"kernel": CUTLASS_REF_KERNEL[dtype], "steps_per_round": n, "rounds": 2,
+            "tflops_cutlass": flop / (min(t_cut) * 1e-3) / 1e12,
+            "tflops_ours_interleaved": flop / (min(t_ours) * 1e-3) / 1e12}
 
 
 def run_reference_cutlass_single_cta(wl):
