@@ -142,6 +142,21 @@ int gemm_sm100a_query(const GemmArgs* args, GemmInfo* info);
 int gemm_sm100a_launch(const GemmArgs* args, void* stream);
 
 /*
+ * gemm_sm100a_launch, fused with an all-gather of D across the GPUs of one
+ * box: the epilogue also stores every element of this launch's D block into
+ * each of `n_peers` (at most 7) further buffers, typically the same block of
+ * the full D on the other GPUs of an N-split, so the gather overlaps the GEMM
+ * instead of following it (replaces the GEMM + ncclAllGather pair the N-split
+ * harness otherwise issues; the reference is single-GPU and has none).
+ * Each peer buffer uses args->ldd and must hold the same m x n block as
+ * args->d.  Peer pointers must be device memory this GPU can reach: the call
+ * enables peer access to other GPUs' memory and returns GEMM_ERR_BAD_ARGS for
+ * host memory, unreachable devices or misaligned pointers.  Only D is
+ * gathered; completion on every GPU means the full D is complete there.
+ */
+int gemm_sm100a_launch_gather(const GemmArgs* args, void* const* peer_d, int32_t n_peers, void* stream);
+
+/*
  * Synchronise `stream`, copy the device status word back and map it to a
  * return code (GEMM_OK or GEMM_ERR_TIMEOUT); *detail (optional) receives the
  * raw word, which encodes the waiting role and pipeline stage.

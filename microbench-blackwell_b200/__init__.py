@@ -61,7 +61,7 @@ class GemmInfo(C.Structure):
 
 # Every symbol include/gemm_sm100a.h declares.
 EXPORTED = (
-    "gemm_sm100a_query", "gemm_sm100a_launch", "gemm_sm100a_read_status",
+    "gemm_sm100a_query", "gemm_sm100a_launch", "gemm_sm100a_launch_gather", "gemm_sm100a_read_status",
     "gemm_sm100a_strerror", "gemm_sm100a_version",
     "gemm_sm100a_generate", "gemm_sm100a_generate_nvfp4", "gemm_sm100a_umma_peak",
 )
@@ -89,6 +89,8 @@ def lib():
         L.gemm_sm100a_query.argtypes = [C.POINTER(GemmArgs), C.POINTER(GemmInfo)]
         L.gemm_sm100a_launch.restype = C.c_int
         L.gemm_sm100a_launch.argtypes = [C.POINTER(GemmArgs), vp]
+        L.gemm_sm100a_launch_gather.restype = C.c_int
+        L.gemm_sm100a_launch_gather.argtypes = [C.POINTER(GemmArgs), C.POINTER(vp), C.c_int32, vp]
         L.gemm_sm100a_read_status.restype = C.c_int
         L.gemm_sm100a_read_status.argtypes = [vp, vp, C.POINTER(i32)]
         L.gemm_sm100a_strerror.restype = C.c_char_p
@@ -149,6 +151,17 @@ def launch(args: GemmArgs, stream: int = 0) -> None:
     if rc != OK:
         _, info = query(args)
         raise GemmError(rc, f"gemm_sm100a_launch ({info.reason.decode()})")
+
+
+def launch_gather(args: GemmArgs, peer_d: list[int], stream: int = 0) -> None:
+    """One GEMM whose epilogue also writes its D block into each buffer of
+    `peer_d` (device addresses, at most 7; e.g. the same block of the full D on
+    the other GPUs of an N-split), fusing the all-gather into the launch."""
+    arr = (C.c_void_p * max(1, len(peer_d)))(*peer_d)
+    rc = lib().gemm_sm100a_launch_gather(C.byref(args), arr, len(peer_d), C.c_void_p(stream))
+    if rc != OK:
+        _, info = query(args)
+        raise GemmError(rc, f"gemm_sm100a_launch_gather ({info.reason.decode() or 'peer pointers'})")
 
 
 def read_status(status_ptr: int, stream: int = 0) -> tuple[int, int]:

@@ -83,6 +83,7 @@ __host__ __device__ constexpr int threads_for(int bn) { return 64 + 32 * epi_war
 constexpr int kSmemLimit = 232448;      // 227 KiB of opt-in dynamic shared memory per CTA
 constexpr int kBarrierBytes = 1024;     // barrier block + bookkeeping words
 constexpr int kMaxStages = 32;
+constexpr int kMaxGatherPeers = 7;   // peer D destinations of the fused gather (8 GPUs per box)
 constexpr int kDefaultL2Prefetch = 0;         // k-blocks of L2 prefetch ahead of the ring (0 = off)
 constexpr int kMinSmemPerCta = 120 * 1024;  // > half of the SM's 228 KiB: at most one CTA per SM
 
@@ -112,6 +113,10 @@ struct KernelParams {
   const uint8_t* sfb;
   int32_t sf_kblocks;     // K / 64 (NVFP4 scale atoms along K)
   int32_t sf_slots;       // NVFP4: TMEM scale-factor slots (stage s uses slot s % sf_slots)
+  // Fused gather: the epilogue also writes every D element to these buffers
+  // (other GPUs' D, reached over NVLink), at the same row/column offsets and ldd.
+  int32_t n_d_peer;
+  __nv_bfloat16* d_peer[kMaxGatherPeers];
   int32_t l2_prefetch;    // k-blocks the L2 prefetch cursor runs ahead of the loads (0 = off)
   int32_t num_acc;        // accumulator buffers in TMEM (2 = epilogue overlaps the next tile)
 };
@@ -604,6 +609,14 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
               if (j < n_valid) *dst = (uint16_t)(j % 2 == 0 ? (pk[j / 2] & 0xFFFFu) : (pk[j / 2] >> 16));
               dst += step;
             }
+            for (int gp = 0; gp < p.n_d_peer; ++gp) {   // fused gather: the same block into each peer D
+              uint16_t* pdst = reinterpret_cast<uint16_t*>(p.d_peer[gp] + row) + col0 * p.ldd;
+#pragma unroll
+              for (int j = 0; j < COLS; ++j) {
+                if (j < n_valid) *pdst = (uint16_t)(j % 2 == 0 ? (pk[j / 2] & 0xFFFFu) : (pk[j / 2] >> 16));
+                pdst += step;
+              }
+            }
           }
         } else {
 #pragma unroll 1
@@ -616,6 +629,14 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
               for (int j = 0; j < 32; ++j) {
                 const int64_t col = n0 + c + j;
                 if (col < p.n) dptr[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+              }
+              for (int gp = 0; gp < p.n_d_peer; ++gp) {
+                __nv_bfloat16* const pp = p.d_peer[gp] + row;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const int64_t col = n0 + c + j;
+                  if (col < p.n) pp[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+                }
               }
             }
           }
@@ -631,6 +652,14 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
             for (int j = 0; j < 16; ++j) {
               const int64_t col = n0 + c + j;
               if (col < p.n) dptr[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+            }
+            for (int gp = 0; gp < p.n_d_peer; ++gp) {
+              __nv_bfloat16* const pp = p.d_peer[gp] + row;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int64_t col = n0 + c + j;
+                if (col < p.n) pp[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+              }
             }
           }
         }
@@ -909,7 +938,9 @@ extern "C" int gemm_sm100a_query(const GemmArgs* args, GemmInfo* info) {
   return rc;
 }
 
-extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
+// One launch; `peers` (n_peers <= kMaxGatherPeers) are extra D destinations
+// already validated by the caller.
+static int launch_impl(const GemmArgs* args, void* const* peers, int n_peers, void* stream) {
   StreamDeviceGuard guard(reinterpret_cast<cudaStream_t>(stream));
   if (!guard.ok) return GEMM_ERR_LAUNCH;
   Resolved r;
@@ -966,6 +997,8 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   p.sfb = reinterpret_cast<const uint8_t*>(a.sfb);
   p.sf_kblocks = (int32_t)(a.k / 64);
   p.sf_slots = r.sf_slots;
+  p.n_d_peer = n_peers;
+  for (int i = 0; i < n_peers; ++i) p.d_peer[i] = reinterpret_cast<__nv_bfloat16*>(peers[i]);
   p.l2_prefetch = a.l2_prefetch < 0 ? 0 : (a.l2_prefetch == 0 ? kDefaultL2Prefetch : a.l2_prefetch);
 
   KernelFn fn = pick_kernel(r.dt, r.cg, r.bn);
@@ -994,6 +1027,38 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
     return GEMM_ERR_LAUNCH;
   }
   return GEMM_OK;
+}
+
+extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
+  return launch_impl(args, nullptr, 0, stream);
+}
+
+extern "C" int gemm_sm100a_launch_gather(const GemmArgs* args, void* const* peer_d, int32_t n_peers,
+                                         void* stream) {
+  if (n_peers < 0 || n_peers > kMaxGatherPeers || (n_peers > 0 && !peer_d)) return GEMM_ERR_BAD_ARGS;
+  StreamDeviceGuard guard(reinterpret_cast<cudaStream_t>(stream));
+  if (!guard.ok) return GEMM_ERR_LAUNCH;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GEMM_ERR_LAUNCH;
+  for (int i = 0; i < n_peers; ++i) {
+    // Every destination must be device memory this GPU can store to; enable
+    // peer access where it is another GPU's memory, so a bad pointer is an
+    // error here and never a fault in the kernel.
+    if (!peer_d[i] || (reinterpret_cast<uintptr_t>(peer_d[i]) & 15)) return GEMM_ERR_BAD_ARGS;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, peer_d[i]) != cudaSuccess || at.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      return GEMM_ERR_BAD_ARGS;
+    }
+    if (at.device != dev) {
+      int can = 0;
+      if (cudaDeviceCanAccessPeer(&can, dev, at.device) != cudaSuccess || !can) { cudaGetLastError(); return GEMM_ERR_BAD_ARGS; }
+      const cudaError_t e = cudaDeviceEnablePeerAccess(at.device, 0);
+      if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) { cudaGetLastError(); return GEMM_ERR_LAUNCH; }
+      cudaGetLastError();   // clear "already enabled"
+    }
+  }
+  return launch_impl(args, peer_d, n_peers, stream);
 }
 
 extern "C" int gemm_sm100a_read_status(const int32_t* status, void* stream, int32_t* detail) {

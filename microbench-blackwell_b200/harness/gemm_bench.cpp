@@ -15,12 +15,16 @@
 //     cannot be implemented (cutlass_gemm_bench.cu:211-224);
 //   * with arguments it runs full problems:
 //         --m M --n N --k K [--init zero|seeded] [--seed S] [--iters I]
-//         [--warmup W] [--check] [--ngpus G] [--allgather] [--raster R]
+//         [--warmup W] [--check] [--ngpus G] [--allgather] [--fused-gather] [--raster R]
 //         [--max-ctas C]
-//     and appends cta_group,ngpus,allgather_ms,relerr to the line.  With
+//     and appends cta_group,ngpus,allgather_ms,relerr (and fused_ms with
+//     --fused-gather) to the line.  With
 //     --ngpus G > 1 the GEMM is split along N (A replicated, B and D
 //     column-sliced; GPU g owns columns [g*N/G, (g+1)*N/G)), timed as the
-//     maximum over GPUs, and --allgather gathers the bf16 D slices into a full
+//     maximum over GPUs; --fused-gather times GEMM + gather in one launch per
+//     GPU (gemm_sm100a_launch_gather: each GPU's epilogue also stores its slice
+//     into every other GPU's full D over NVLink) and checks the gathered D
+//     bitwise against the slices; --allgather gathers the bf16 D slices into a full
 //     D on every GPU with one ncclAllGather (timed separately).
 //
 // All GEMM work goes through the C ABI (gemm_sm100a_launch); the harness
@@ -104,6 +108,7 @@ struct Options {
   bool check = false;
   int ngpus = 1;
   bool allgather = false;
+  bool fused_gather = false;
   int raster = 0;
   int max_ctas = -1;           // -1: single CTA (pair) in reference mode, all SMs otherwise
 };
@@ -127,6 +132,7 @@ static Options parse(int argc, char** argv) {
     else if (a == "--check") { o.check = true; }
     else if (a == "--ngpus") { o.ngpus = atoi(next()); o.full = true; }
     else if (a == "--allgather") { o.allgather = true; }
+    else if (a == "--fused-gather") { o.fused_gather = true; }
     else if (a == "--raster") { o.raster = atoi(next()); }
     else if (a == "--max-ctas") { o.max_ctas = atoi(next()); }
     else { fprintf(stderr, "unknown argument %s\n", a.c_str()); exit(2); }
@@ -159,6 +165,7 @@ struct DeviceGemm {
   cudaStream_t stream = nullptr;
   int64_t n_local = 0, n0 = 0;
   void *a = nullptr, *b = nullptr, *d = nullptr, *sfa = nullptr, *sfb = nullptr, *dfull = nullptr;
+  void* dfused = nullptr;   // full M x N D written by every GPU's fused-gather launch
   int32_t* status = nullptr;
   GemmArgs args{};
   cudaEvent_t e0{}, e1{}, g0{}, g1{};
@@ -297,6 +304,66 @@ int main(int argc, char** argv) {
     for (auto& c : comms) ncclCommDestroy(c);
   }
 
+  // ---------------------------------------------------------------- optional fused GEMM + gather
+  float fused_ms = 0.0f;
+  if (o.fused_gather && o.ngpus > 1) {
+    if (o.ngpus - 1 > 7) { fprintf(stderr, "--fused-gather supports up to 8 GPUs\n"); return 1; }
+    for (auto& x : g) { CK(cudaSetDevice(x.dev)); CK(cudaMalloc(&x.dfused, (size_t)o.m * o.n * 2)); }
+    std::vector<std::vector<void*>> peers(o.ngpus);
+    std::vector<GemmArgs> fargs(o.ngpus);
+    for (auto& x : g) {
+      fargs[x.dev] = x.args;
+      fargs[x.dev].d = (uint16_t*)x.dfused + x.n0 * o.m;             // this GPU's slice of its full D
+      for (auto& y : g)
+        if (y.dev != x.dev) peers[x.dev].push_back((uint16_t*)y.dfused + x.n0 * o.m);   // same slice, peers' D
+    }
+    auto launch_fused = [&]() {
+      for (auto& x : g) {
+        CK(cudaSetDevice(x.dev));
+        int rc = gemm_sm100a_launch_gather(&fargs[x.dev], peers[x.dev].data(), (int32_t)peers[x.dev].size(), x.stream);
+        if (rc != GEMM_OK) { fprintf(stderr, "fused launch failed: %s\n", gemm_sm100a_strerror(rc)); exit(1); }
+      }
+    };
+    auto sync_all = [&]() { for (auto& x : g) { CK(cudaSetDevice(x.dev)); CK(cudaStreamSynchronize(x.stream)); } };
+    for (int w = 0; w < std::max(1, o.warmup); ++w) launch_fused();
+    sync_all();
+    // Every GPU finished its warm-up stores into every D before timing starts.
+    for (auto& x : g) { CK(cudaSetDevice(x.dev)); CK(cudaEventRecord(x.g0, x.stream)); }
+    // GPU x only ever writes slice x (of every D), so back-to-back launches
+    // need no cross-GPU ordering; each GPU's time includes its remote stores.
+    for (int it = 0; it < o.iters; ++it) launch_fused();
+    for (auto& x : g) { CK(cudaSetDevice(x.dev)); CK(cudaEventRecord(x.g1, x.stream)); }
+    for (auto& x : g) {
+      CK(cudaSetDevice(x.dev));
+      CK(cudaEventSynchronize(x.g1));
+      float ms = 0.0f;
+      CK(cudaEventElapsedTime(&ms, x.g0, x.g1));
+      fused_ms = std::max(fused_ms, ms / o.iters);
+      int32_t detail = 0;
+      if (gemm_sm100a_read_status(x.status, x.stream, &detail) != GEMM_OK) {
+        fprintf(stderr, "device wait timed out on GPU %d (status 0x%08x)\n", x.dev, (unsigned)detail);
+        return 1;
+      }
+    }
+    // Bitwise check: sampled columns of every slice, on every GPU, against the
+    // owner's own result from the plain launches above.
+    std::mt19937_64 rng(o.seed + 777);
+    std::vector<uint16_t> got(o.m), want(o.m);
+    for (auto& x : g)
+      for (auto& y : g)
+        for (int sidx = 0; sidx < 10; ++sidx) {
+          const int64_t cl = sidx == 0 ? 0 : (sidx == 1 ? n_local - 1 : (int64_t)(rng() % (uint64_t)n_local));
+          CK(cudaSetDevice(x.dev));
+          CK(cudaMemcpy(got.data(), (uint16_t*)x.dfused + (y.n0 + cl) * o.m, (size_t)o.m * 2, cudaMemcpyDeviceToHost));
+          CK(cudaSetDevice(y.dev));
+          CK(cudaMemcpy(want.data(), (uint16_t*)y.d + cl * o.m, (size_t)o.m * 2, cudaMemcpyDeviceToHost));
+          if (memcmp(got.data(), want.data(), (size_t)o.m * 2) != 0) {
+            fprintf(stderr, "fused gather mismatch: GPU %d, slice of GPU %d, column %lld\n", x.dev, y.dev, (long long)cl);
+            return 1;
+          }
+        }
+  }
+
   // ---------------------------------------------------------------- optional sampled fp64 check
   double relerr = -1.0;
   if (o.check) {
@@ -361,6 +428,7 @@ int main(int argc, char** argv) {
   std::cout << o.m << "," << o.n << "," << o.k << "," << TILE_M << "," << TILE_N << "," << TILE_K << ","
             << STAGES << "," << kDtype << "," << avg_ms << "," << tflops;
   if (o.full) std::cout << "," << CTA_GROUP << "," << o.ngpus << "," << ag_ms << "," << relerr;
+  if (o.full && o.fused_gather) std::cout << "," << fused_ms;
   std::cout << std::endl;
 
   for (auto& x : g) {
@@ -369,6 +437,7 @@ int main(int argc, char** argv) {
     if (x.sfa) cudaFree(x.sfa);
     if (x.sfb) cudaFree(x.sfb);
     if (x.dfull) cudaFree(x.dfull);
+    if (x.dfused) cudaFree(x.dfused);
   }
   if (o.check && relerr > (DTYPE_ID == 2 ? 1e-2 : 2e-3)) {
     fprintf(stderr, "check failed: relative Frobenius error %.3e\n", relerr);
