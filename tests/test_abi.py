@@ -153,3 +153,14 @@ def test_launch_rejects_before_touching_the_gpu(pkg):
     with pytest.raises(pkg.GemmError) as e:
         pkg.launch(_args(pkg, stages=7, tile_n=256))
     assert e.value.code == pkg.ERR_CANNOT_IMPLEMENT
+
+
+def test_gather_rejects_bad_destination_lists_before_any_cuda_call(pkg):
+    """gemm_sm100a_launch_gather: at most 7 extra destinations, and a list when any."""
+    import ctypes as C
+    L = pkg.lib()
+    args = _args(pkg)
+    arr = (C.c_void_p * 8)(*([0x10000] * 8))
+    assert L.gemm_sm100a_launch_gather(C.byref(args), arr, 8, None) == pkg.ERR_BAD_ARGS
+    assert L.gemm_sm100a_launch_gather(C.byref(args), None, 1, None) == pkg.ERR_BAD_ARGS
+    assert L.gemm_sm100a_launch_gather(C.byref(args), arr, -1, None) == pkg.ERR_BAD_ARGS
