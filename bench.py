@@ -299,10 +299,11 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
                                 b_dist=dist_code(pkg, wl["b"][0]), b_scale=wl["b"][1],
                                 n0=n0, device=dev, stream=st)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
+    clock_buf = torch.zeros(2, dtype=torch.int64, device=dev)     # CTA 0's [cycles, ns] per launch
     gargs = pkg.make_args(dtype=dt, m=m, n=n, k=k, a=ops.a.data_ptr(), b=ops.b.data_ptr(),
                           d=ops.d.data_ptr(), sfa=None if ops.sfa is None else ops.sfa.data_ptr(),
                           sfb=None if ops.sfb is None else ops.sfb.data_ptr(),
-                          status=status.data_ptr(), **knobs)
+                          status=status.data_ptr(), clock_out=clock_buf.data_ptr(), **knobs)
     rc, info = pkg.query(gargs)
     if rc != pkg.OK:
         raise SystemExit(f"cannot implement: {info.reason.decode()}")
@@ -347,6 +348,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     value = flop * world / (ms_per_step * 1e-3) / 1e12
     achieved = flop / (ms / args.steps * 1e-3) / 1e12          # this rank's kernel, per launch
     clocks = sampler.summary()
+    clocks["kernel_sm_mhz"] = kernel_mhz(clock_buf)
 
     # ---------------------------------------------------------- optional all-gather of D (N > 1)
     allgather = None
@@ -410,8 +412,9 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
                      "umma_peak_tflops": umma_peak["tflops"], "umma_flop_per_clk_per_sm": umma_peak["flop_per_clk_per_sm"],
                      "umma_sm_mhz": umma_peak["sm_mhz"], "source": umma_peak["source"],
                      "reference_flop_per_clk_per_sm": REF_UMMA_FLOP_PER_CLK_SM[wl["dtype"]],
-                     "pct_at_gemm_clock": (100.0 * achieved / (umma_peak["flop_per_clk_per_sm"] * 148 * sm_mhz * 1e6 / 1e12))
-                     if sm_mhz else None},
+                     "pct_at_gemm_clock": pct_at_clock(achieved, umma_peak, clocks["kernel_sm_mhz"]),
+                     "gemm_sm_mhz": clocks["kernel_sm_mhz"],
+                     "pct_at_max_clock": 100.0 * achieved / (umma_peak["flop_per_clk_per_sm"] * 148 * SM_MAX_MHZ * 1e6 / 1e12)},
         "clocks": clocks,
         "e2e": e2e,
         "gpu_launches": args.steps,
@@ -433,6 +436,20 @@ PER_DTYPE = [
     ("nvfp4_config4", "nvfp4_mlp", "weak"),
     ("e4m3_nsplit_config5", "e4m3_nsplit", "strong"),
 ]
+
+
+def kernel_mhz(clock_buf):
+    """Effective SM clock of the last launch, from the kernel's own clock64 / %globaltimer
+    record (CTA 0, whole launch): sampled NVML clocks miss power-cap throttling."""
+    cyc, ns = (int(v) for v in clock_buf.cpu().tolist())
+    return 1000.0 * cyc / ns if ns > 0 else None
+
+
+def pct_at_clock(tflops, umma_peak, mhz):
+    """% of the probe's FLOP/clk/SM x 148 SMs at the GEMM's own clock: the per-clock efficiency."""
+    if not mhz:
+        return None
+    return 100.0 * tflops / (umma_peak["flop_per_clk_per_sm"] * 148 * mhz * 1e6 / 1e12)
 
 
 def measured_umma_peak(pkg, dtype_name: str, dev) -> dict:
@@ -465,9 +482,11 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
         ops = pkg.make_operands(dt, m, n, k, seed=args.seed, a_dist=dist_code(pkg, wl["a"][0]), a_scale=wl["a"][1],
                                 b_dist=dist_code(pkg, wl["b"][0]), b_scale=wl["b"][1], n0=slab.n0,
                                 device=dev, stream=stream.cuda_stream)
+        clock_buf = torch.zeros(2, dtype=torch.int64, device=dev)
         g = pkg.make_args(dtype=dt, m=m, n=n, k=k, a=ops.a.data_ptr(), b=ops.b.data_ptr(), d=ops.d.data_ptr(),
                           sfa=None if ops.sfa is None else ops.sfa.data_ptr(),
-                          sfb=None if ops.sfb is None else ops.sfb.data_ptr(), **wl["knobs"])
+                          sfb=None if ops.sfb is None else ops.sfb.data_ptr(), clock_out=clock_buf.data_ptr(),
+                          **wl["knobs"])
         L = pkg.lib()
         sp = C.c_void_p(stream.cuda_stream)
         # Untimed settle (>= 3 launches, ~0.25 s): the clock reaches this configuration's
@@ -488,6 +507,7 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
         s1.record(stream)
         s1.synchronize()
         ms = nsplit.max_over_ranks(s0.elapsed_time(s1) / steps, device=dev)
+        gemm_mhz = kernel_mhz(clock_buf)
         flop_total = pkg.flops(m, n, k) * world
         tf = flop_total / (ms * 1e-3) / 1e12
         per_gpu = tf / world
@@ -498,6 +518,11 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
                       "ms_per_step": ms, "tflops": tf, "tflops_per_gpu": per_gpu,
                       "umma_peak_tflops": peak["tflops"], "umma_peak_sm_mhz": peak["sm_mhz"],
                       "pct_measured_umma_peak": 100.0 * per_gpu / peak["tflops"],
+                      # The probe's clock under power capping can fall below the GEMM's, which
+                      # lifts the ratio above 100 %; this one uses the SM's maximum clock instead.
+                      "pct_umma_peak_at_max_clock": 100.0 * per_gpu / (peak["flop_per_clk_per_sm"] * 148 * SM_MAX_MHZ * 1e6 / 1e12),
+                      "gemm_sm_mhz": gemm_mhz,
+                      "pct_umma_peak_at_gemm_clock": pct_at_clock(per_gpu, peak, gemm_mhz),
                       "reference_cutlass_full": ref_full}
         del ops
         torch.cuda.empty_cache()
@@ -612,6 +637,8 @@ def run_single_cta(pkg, wl, dev, stream):
     out["binary"] = binp.name
     return out
 
+
+SM_MAX_MHZ = 1965.0   # B200 clocks.max.sm
 
 CUTLASS_REF_KERNEL = {"bf16": "CUTLASS SM100 1SM 128x256x64, 4 stages (cutlass_gemm_mainloop/results.csv:461)",
                       "e4m3": "CUTLASS SM100 1SM 128x256x128, auto stages (cutlass_gemm_mainloop/results.csv:938)"}

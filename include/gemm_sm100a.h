@@ -106,6 +106,8 @@ typedef struct GemmArgs {
   uint32_t timeout_ms;    /* device wait budget; 0 = default (4000 ms) */
   uint32_t flags;         /* GEMM_FLAG_* */
   int32_t  l2_prefetch;   /* warm L2 this many k-blocks ahead of the shared-memory ring; 0 = default, < 0 = off */
+  unsigned long long* clock_out; /* optional device [2]: SM cycles and nanoseconds CTA 0 spent in the launch
+                                    (cycles / ns = the effective SM clock under power capping) */
 } GemmArgs;
 
 /* What a launch would do; filled by gemm_sm100a_query. */

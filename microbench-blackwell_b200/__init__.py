@@ -45,6 +45,7 @@ class GemmArgs(C.Structure):
         ("raster_group", C.c_int32),
         ("status", C.c_void_p), ("timeout_ms", C.c_uint32), ("flags", C.c_uint32),
         ("l2_prefetch", C.c_int32),
+        ("clock_out", C.c_void_p),
     ]
 
 
@@ -120,7 +121,7 @@ def make_args(*, dtype: int, m: int, n: int, k: int, a: int, b: int, d: int,
               tile_m: int = 0, tile_n: int = 0, tile_k: int = 0, stages: int = 0,
               cta_group: int = 0, cluster_m: int = 0, max_ctas: int = 0, raster_group: int = 0,
               status: int | None = None, timeout_ms: int = 0, flags: int = 0,
-              l2_prefetch: int = 0) -> GemmArgs:
+              l2_prefetch: int = 0, clock_out: int | None = None) -> GemmArgs:
     """GemmArgs from raw device addresses (ints).  Leading dimensions default to packed."""
     g = GemmArgs()
     g.struct_size = C.sizeof(GemmArgs)
@@ -136,6 +137,7 @@ def make_args(*, dtype: int, m: int, n: int, k: int, a: int, b: int, d: int,
     g.status = status
     g.timeout_ms, g.flags = timeout_ms, flags
     g.l2_prefetch = l2_prefetch
+    g.clock_out = clock_out
     return g
 
 

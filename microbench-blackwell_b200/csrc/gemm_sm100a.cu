@@ -118,6 +118,7 @@ struct KernelParams {
   int32_t n_d_peer;
   __nv_bfloat16* d_peer[kMaxGatherPeers];
   int32_t l2_prefetch;    // k-blocks the L2 prefetch cursor runs ahead of the loads (0 = off)
+  unsigned long long* clock_out;   // optional: CTA 0's [cycles, ns] over the launch
   int32_t num_acc;        // accumulator buffers in TMEM (2 = epilogue overlaps the next tile)
 };
 
@@ -271,6 +272,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
   const int pair = (int)(blockIdx.x / CG);
   const int num_pairs = (int)(gridDim.x / CG);
 
+  const unsigned long long clk0 = clock64(), ns0 = globaltimer_ns();
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b);
@@ -685,6 +687,10 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     tc_fence_after();
     tmem_dealloc<CG>(tmem_base, (uint32_t)p.tmem_cols);
   }
+  if (p.clock_out && blockIdx.x == 0 && threadIdx.x == 0) {
+    p.clock_out[0] = clock64() - clk0;
+    p.clock_out[1] = globaltimer_ns() - ns0;
+  }
 }
 
 // ----------------------------------------------------------------------------
@@ -1001,6 +1007,7 @@ static int launch_impl(const GemmArgs* args, void* const* peers, int n_peers, vo
   p.n_d_peer = n_peers;
   for (int i = 0; i < n_peers; ++i) p.d_peer[i] = reinterpret_cast<__nv_bfloat16*>(peers[i]);
   p.l2_prefetch = a.l2_prefetch < 0 ? 0 : (a.l2_prefetch == 0 ? kDefaultL2Prefetch : a.l2_prefetch);
+  p.clock_out = a.clock_out;
 
   KernelFn fn = pick_kernel(r.dt, r.cg, r.bn);
   if (!fn) return GEMM_ERR_CANNOT_IMPLEMENT;
