@@ -431,11 +431,17 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           if (++stage == n_stages) { stage = 0; phase ^= 1u; }
         }
       }
-      if (!ok && CG == 1) {
-        // Let every load already issued land before the CTA may exit.
+      if (!ok && (CG == 1 || leader)) {
+        // Let every load already issued land before the CTA may exit.  In a
+        // pair the leader's full barrier of a stage completes only when both
+        // CTAs' loads of that stage have landed, so the leader's drain also
+        // covers its peer's loads; the teardown cluster barrier then keeps the
+        // peer resident until the drain is over.
         for (int s = 0; s < n_stages; ++s)
           if (issued_mask & (1u << s)) drain_wait(full_bar + 8u * s, (issued_parity >> s) & 1u, 100000000ull);
       } else if (!ok) {
+        // Pair peer: its loads complete on the leader's barriers, which it
+        // cannot wait on; give them a short fixed window before the teardown barrier.
         const uint64_t t0 = globaltimer_ns();
         while (globaltimer_ns() - t0 < 2000000ull) {}
       }
@@ -1041,6 +1047,36 @@ extern "C" int gemm_sm100a_launch(const GemmArgs* args, void* stream) {
   return launch_impl(args, nullptr, 0, stream);
 }
 
+namespace {
+
+using PFN_memGetAddressRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+PFN_memGetAddressRange g_addr_range = nullptr;
+std::once_flag g_addr_range_once;
+
+// True when [ptr, ptr + bytes) lies inside one device allocation.  The range
+// is queried with the owning device current (its primary context), then the
+// caller's device is restored.
+bool block_inside_allocation(const void* ptr, size_t bytes, int owner, int current) {
+  std::call_once(g_addr_range_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_addr_range = reinterpret_cast<PFN_memGetAddressRange>(fn);
+  });
+  if (!g_addr_range) return false;
+  if (owner != current && cudaSetDevice(owner) != cudaSuccess) { cudaGetLastError(); return false; }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const CUresult r = g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (owner != current) cudaSetDevice(current);
+  if (r != CUDA_SUCCESS) return false;
+  const uintptr_t p = reinterpret_cast<uintptr_t>(ptr);
+  return p >= base && bytes <= size && p - base <= size - bytes;
+}
+
+}  // namespace
+
 extern "C" int gemm_sm100a_launch_gather(const GemmArgs* args, void* const* peer_d, int32_t n_peers,
                                          void* stream) {
   if (n_peers < 0 || n_peers > kMaxGatherPeers || (n_peers > 0 && !peer_d)) return GEMM_ERR_BAD_ARGS;
@@ -1048,13 +1084,33 @@ extern "C" int gemm_sm100a_launch_gather(const GemmArgs* args, void* const* peer
   if (!guard.ok) return GEMM_ERR_LAUNCH;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return GEMM_ERR_LAUNCH;
+  {
+    Resolved r;
+    const int rc = resolve(args, r);
+    if (rc != GEMM_OK) return rc;
+  }
+  // Bytes of the m x n column-major block at stride ldd that every destination must hold.
+  const size_t block_bytes = ((size_t)(args->n - 1) * (size_t)args->ldd + (size_t)args->m) * 2u;
+  if (n_peers > 0) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, args->d) != cudaSuccess || at.type != cudaMemoryTypeDevice ||
+        !block_inside_allocation(args->d, block_bytes, at.device, dev)) {
+      cudaGetLastError();
+      return GEMM_ERR_BAD_ARGS;
+    }
+  }
   for (int i = 0; i < n_peers; ++i) {
-    // Every destination must be device memory this GPU can store to; enable
-    // peer access where it is another GPU's memory, so a bad pointer is an
-    // error here and never a fault in the kernel.
+    // Every destination must be device memory this GPU can store to, large
+    // enough for the whole block; enable peer access where it is another
+    // GPU's memory, so a bad pointer or a short buffer is an error here and
+    // never a fault in the kernel.
     if (!peer_d[i] || (reinterpret_cast<uintptr_t>(peer_d[i]) & 15)) return GEMM_ERR_BAD_ARGS;
     cudaPointerAttributes at;
     if (cudaPointerGetAttributes(&at, peer_d[i]) != cudaSuccess || at.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      return GEMM_ERR_BAD_ARGS;
+    }
+    if (!block_inside_allocation(peer_d[i], block_bytes, at.device, dev)) {
       cudaGetLastError();
       return GEMM_ERR_BAD_ARGS;
     }

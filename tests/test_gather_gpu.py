@@ -21,11 +21,13 @@ def _args(pkg, ops, d_ptr, **knobs):
                          sfb=None if ops.sfb is None else ops.sfb.data_ptr(), **knobs)
 
 
+@pytest.mark.parametrize("n", [1536, 1500])                                      # whole tiles, and an N tail
 @pytest.mark.parametrize("knobs", [dict(cta_group=2, tile_n=512, tile_k=64),    # one accumulator: staged epilogue
                                    dict(cta_group=1, tile_n=256, tile_k=64),    # double-buffered epilogue
-                                   dict(cta_group=1, tile_n=16, tile_k=64)])    # 16-column chunks
-def test_extra_destinations_on_one_gpu_match_d(pkg, cuda, knobs):
-    m, n, k = 512, 1536, 1024
+                                   dict(cta_group=1, tile_n=16, tile_k=64),     # 16-column chunks
+                                   dict(cta_group=1, tile_m=64, tile_n=256, tile_k=64)])  # M = 64 lane layout
+def test_extra_destinations_on_one_gpu_match_d(pkg, cuda, knobs, n):
+    m, k = 512, 1024
     ops = pkg.make_operands(pkg.BF16, m, n, k, seed=3, device=cuda)
     extra = [torch.full_like(ops.d, 7) for _ in range(2)]
     st = torch.cuda.current_stream().cuda_stream
@@ -45,12 +47,25 @@ def test_bad_destinations_are_rejected_before_launch(pkg, cuda):
     st = torch.cuda.current_stream().cuda_stream
     L = pkg.lib()
     host = np.zeros(256 * 256, dtype=np.uint16)
+    # Exact-size allocations (torch's caching allocator would hand out slices of larger segments).
+    from cuda.bindings import runtime as rt
+    err, short = rt.cudaMalloc(256 * 256)             # half of the 256 x 256 bf16 block
+    assert err == rt.cudaError_t.cudaSuccess
+    err, exact = rt.cudaMalloc(256 * 256 * 2)         # exactly one block
+    assert err == rt.cudaError_t.cudaSuccess
     for peers, n in [([host.ctypes.data], 1),                     # host memory
                      ([ops.d.data_ptr() + 2], 1),                 # not 16-byte aligned
-                     ([ops.d.data_ptr()] * 8, 8)]:                # more than 7 destinations
+                     ([ops.d.data_ptr()] * 8, 8),                 # more than 7 destinations
+                     ([int(short)], 1),                           # allocation shorter than the block
+                     ([int(exact) + 64 * 256 * 2], 1)]:           # block runs past the end of its allocation
         arr = (C.c_void_p * len(peers))(*peers)
         assert L.gemm_sm100a_launch_gather(C.byref(args), arr, n, C.c_void_p(st)) == pkg.ERR_BAD_ARGS
+    # the exact allocation itself is accepted
+    arr = (C.c_void_p * 1)(int(exact))
+    assert L.gemm_sm100a_launch_gather(C.byref(args), arr, 1, C.c_void_p(st)) == pkg.OK
     torch.cuda.synchronize()
+    rt.cudaFree(short)
+    rt.cudaFree(exact)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
