@@ -369,7 +369,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
         del full
 
     # ---------------------------------------------------------- the reference's kernel family, same box
-    ref_full = run_reference_cutlass_full(pkg, ops, gargs, stream, wl["dtype"], args.steps)
+    ref_full = run_reference_cutlass_full(pkg, ops, gargs, stream, wl["dtype"], args.steps) if world == 1 else None
 
     # ---------------------------------------------------------- end to end (host buffers)
     e2e = run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank)
@@ -511,7 +511,7 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
         flop_total = pkg.flops(m, n, k) * world
         tf = flop_total / (ms * 1e-3) / 1e12
         per_gpu = tf / world
-        ref_full = run_reference_cutlass_full(pkg, ops, g, stream, wl["dtype"], steps)
+        ref_full = run_reference_cutlass_full(pkg, ops, g, stream, wl["dtype"], steps) if world == 1 else None
         peak = measured_umma_peak(pkg, wl["dtype"], dev)
         out[label] = {"workload": name, "baseline_config": wl["config"], "scaling": scaling,
                       "m": m, "n_total": n * world, "k": k, "knobs": wl["knobs"], "steps": steps,
@@ -640,33 +640,38 @@ def run_single_cta(pkg, wl, dev, stream):
 
 SM_MAX_MHZ = 1965.0   # B200 clocks.max.sm
 
-CUTLASS_REF_KERNEL = {"bf16": "CUTLASS SM100 1SM 128x256x64, 4 stages (cutlass_gemm_mainloop/results.csv:461)",
-                      "e4m3": "CUTLASS SM100 1SM 128x256x128, auto stages (cutlass_gemm_mainloop/results.csv:938)"}
+# Kernels of oracle/_ref/libcutlass_ref.so (oracle/cutlass_ref.cu) timed beside ours, per dtype.
+CUTLASS_REF_KERNELS = {
+    "bf16": {0: "CUTLASS SM100 1SM 128x256x64, 4 stages (the reference's best point, cutlass_gemm_mainloop/results.csv:461)",
+             2: "CUTLASS SM100 2SM 256x256x64, cluster 2x1, auto stages, TMA epilogue"},
+    "e4m3": {1: "CUTLASS SM100 1SM 128x256x128, auto stages (cutlass_gemm_mainloop/results.csv:938)",
+             3: "CUTLASS SM100 2SM 256x256x128, cluster 2x1, auto stages, TMA epilogue"},
+    "nvfp4": {4: "CUTLASS SM100 1SM Nvf4 128x256x256, auto stages",
+              5: "CUTLASS SM100 2SM Nvf4 256x256x256, cluster 2x1, auto stages"},
+}
 
 
 def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
-    """The reference's own CUTLASS kernel family at its best tile (oracle/_ref/libcutlass_ref.so,
-    the cutlass_gemm_bench.cu:101-156 type chain) on the same operands over the whole GPU,
-    timed interleaved with ours (2 rounds each) so both see the same clock state.
-    Informational: the reference itself only runs one CTA."""
+    """The reference's own CUTLASS kernel family (oracle/_ref/libcutlass_ref.so, the
+    cutlass_gemm_bench.cu:101-156 type chain, plus its 2SM and Nvf4 schedules) on the same
+    operands over the whole GPU, each kernel timed interleaved with ours (2 rounds each)
+    so both see the same clock state.  Informational: the reference itself runs one CTA."""
     import torch
-    code = {"bf16": 0, "e4m3": 1}.get(dtype)
+    kernels = CUTLASS_REF_KERNELS.get(dtype)
     lib = ROOT / "oracle" / "_ref" / "libcutlass_ref.so"
-    if code is None:
+    if kernels is None:
         return None
     if not lib.exists():
-        return {"unavailable": "oracle/_ref/libcutlass_ref.so not built (oracle/ref_build.sh needs the reference tree)"}
+        return {"unavailable": "oracle/_ref/libcutlass_ref.so not built (oracle/ref_build.sh)"}
     R = C.CDLL(str(lib))
-    R.cutlass_ref_gemm.restype = C.c_int
-    R.cutlass_ref_gemm.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
-                                   C.c_int, C.c_void_p]
+    R.cutlass_ref_run.restype = C.c_int
+    R.cutlass_ref_run.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                  C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
     L = pkg.lib()
     sp = C.c_void_p(stream.cuda_stream)
     d_ref = torch.empty_like(ops.d)
-
-    def cut():
-        return R.cutlass_ref_gemm(code, ops.a.data_ptr(), ops.b.data_ptr(), d_ref.data_ptr(),
-                                  ops.m, ops.n, ops.k, 0, sp)
+    sfa = None if ops.sfa is None else ops.sfa.data_ptr()
+    sfb = None if ops.sfb is None else ops.sfb.data_ptr()
 
     def ours():
         return L.gemm_sm100a_launch(C.byref(gargs), sp)
@@ -681,22 +686,40 @@ def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
         e1.synchronize()
         return e0.elapsed_time(e1) / n
 
-    for _ in range(3):
-        if cut() != 0:
-            return {"unavailable": "cutlass_ref_gemm cannot run this problem"}
-        ours()
-    stream.synchronize()
-    n = max(5, min(steps, 50))
-    t_cut, t_ours = [], []
-    for _ in range(2):
-        t_ours.append(timed(ours, n))
-        t_cut.append(timed(cut, n))
-    if None in t_cut or None in t_ours:
-        return {"unavailable": "launch failed"}
     flop = pkg.flops(ops.m, ops.n, ops.k)
-    return {"kernel": CUTLASS_REF_KERNEL[dtype], "steps_per_round": n, "rounds": 2,
-            "tflops_cutlass": flop / (min(t_cut) * 1e-3) / 1e12,
-            "tflops_ours_interleaved": flop / (min(t_ours) * 1e-3) / 1e12}
+    n = max(5, min(steps, 50))
+    out = {"steps_per_round": n, "rounds": 2, "kernels": {}}
+    best = None
+    for kid, desc in kernels.items():
+        def cut(kid=kid):
+            return R.cutlass_ref_run(kid, ops.a.data_ptr(), ops.b.data_ptr(), sfa, sfb, d_ref.data_ptr(),
+                                     ops.m, ops.n, ops.k, 0, sp)
+        rc = cut()
+        if rc != 0:
+            out["kernels"][desc] = {"unavailable": f"cutlass_ref_run returned {rc}"}
+            continue
+        for _ in range(2):
+            cut(); ours()
+        stream.synchronize()
+        t_cut, t_ours = [], []
+        for _ in range(2):
+            t_ours.append(timed(ours, n))
+            t_cut.append(timed(cut, n))
+        if None in t_cut or None in t_ours:
+            out["kernels"][desc] = {"unavailable": "launch failed"}
+            continue
+        rec = {"tflops_cutlass": flop / (min(t_cut) * 1e-3) / 1e12,
+               "tflops_ours_interleaved": flop / (min(t_ours) * 1e-3) / 1e12}
+        rec["ours_over_cutlass"] = rec["tflops_ours_interleaved"] / rec["tflops_cutlass"]
+        out["kernels"][desc] = rec
+        if best is None or rec["tflops_cutlass"] > best[1]["tflops_cutlass"]:
+            best = (desc, rec)
+    if best is not None:
+        out["best_cutlass_kernel"] = best[0]
+        out["tflops_cutlass"] = best[1]["tflops_cutlass"]
+        out["tflops_ours_interleaved"] = best[1]["tflops_ours_interleaved"]
+        out["ours_over_best_cutlass"] = best[1]["ours_over_cutlass"]
+    return out
 
 
 def run_reference_cutlass_single_cta(wl):

@@ -7,7 +7,9 @@
  * Gemm::can_implement / initialize / run (cutlass_gemm_bench.cu:206-239).
  * The math is the reference's:
  *
- *     D = alpha * (A . B^T)      (beta = 0, no C source; cutlass_gemm_bench.cu:117-118,196-204)
+ *     D = alpha * (A . B^T) + beta * C      (the reference runs beta = 0 with no C source,
+ *                                            cutlass_gemm_bench.cu:117-118,196-204; its
+ *                                            LinearCombination epilogue also takes beta and C)
  *
  *   A  M x K, row-major   (K contiguous)      cutlass_gemm_bench.cu:103 LayoutA = RowMajor
  *   B  N x K, "K-major"   (K contiguous)      cutlass_gemm_bench.cu:104 LayoutB = ColumnMajor (K x N)
@@ -50,12 +52,23 @@ enum {
   GEMM_ERR_BAD_ARGS     = -4       /* null pointer, struct-size mismatch */
 };
 
+/* Layout of D (and C): the reference's LayoutD is column-major
+ * (cutlass_gemm_bench.cu:105); row-major is the other LinearCombination layout. */
+enum {
+  GEMM_LAYOUT_COL_MAJOR = 0,   /* M contiguous, element (i, j) at i + j * ld */
+  GEMM_LAYOUT_ROW_MAJOR = 1    /* N contiguous, element (i, j) at i * ld + j */
+};
+
 /* Flags. */
 enum {
   /* Fault injection for tests of the timeout path: the producer warp issues
    * no loads, so every consumer wait runs out after timeout_ms and the kernel
    * records GEMM_ERR_TIMEOUT in *status and returns.  Never used for timing. */
-  GEMM_FLAG_INJECT_STALL = 1u << 0
+  GEMM_FLAG_INJECT_STALL = 1u << 0,
+  /* Store D straight from registers instead of staging each chunk in shared
+   * memory for a TMA store (the fallback when the staging buffers do not fit
+   * next to the ring); for comparisons of the two epilogues. */
+  GEMM_FLAG_DIRECT_EPILOGUE = 1u << 1
 };
 
 /*
@@ -108,6 +121,16 @@ typedef struct GemmArgs {
   int32_t  l2_prefetch;   /* warm L2 this many k-blocks ahead of the shared-memory ring; 0 = default, < 0 = off */
   unsigned long long* clock_out; /* optional device [2]: SM cycles and nanoseconds CTA 0 spent in the launch
                                     (cycles / ns = the effective SM clock under power capping) */
+  /* Epilogue (CUTLASS LinearCombination, cutlass_gemm_bench.cu:117-118,196-204):
+   * D = alpha * scale_a * scale_b * (A . B^T) + beta * C, computed in fp32 and
+   * rounded once to bf16.  C is bf16 with D's layout and leading dimension ldc
+   * (16-byte aligned, ldc a multiple of 8), read only when beta != 0; C may be D. */
+  float    beta;          /* 0 in the reference */
+  const void* c;          /* bf16 C, or NULL when beta == 0 */
+  int64_t  ldc;
+  int32_t  d_layout;      /* GEMM_LAYOUT_*; 0 = column-major as in the reference */
+  float    scale_a;       /* per-tensor dequantisation scale of A (fp8: "per-tensor fp32 scale"); 0 means 1.0 */
+  float    scale_b;       /* per-tensor scale of B; 0 means 1.0 */
 } GemmArgs;
 
 /* What a launch would do; filled by gemm_sm100a_query. */
@@ -123,6 +146,8 @@ typedef struct GemmInfo {
   int32_t  num_sms;
   int32_t  can_implement;        /* 1 if gemm_sm100a_launch would accept the arguments */
   char     reason[128];          /* why not, when can_implement == 0 */
+  int32_t  epilogue_staging_buffers; /* shared-memory staging buffers per epilogue group (TMA-store
+                                        epilogue); 0 = D stored directly from registers */
 } GemmInfo;
 
 /*
@@ -151,7 +176,8 @@ int gemm_sm100a_launch(const GemmArgs* args, void* stream);
  * instead of following it (replaces the GEMM + ncclAllGather pair the N-split
  * harness otherwise issues; the reference is single-GPU and has none).
  * Each peer buffer uses args->ldd and must hold the same m x n block as
- * args->d.  Peer pointers must be device memory this GPU can reach: the call
+ * args->d (checked against its allocation before the launch); D must be
+ * column-major (GEMM_ERR_CANNOT_IMPLEMENT otherwise).  Peer pointers must be device memory this GPU can reach: the call
  * enables peer access to other GPUs' memory and returns GEMM_ERR_BAD_ARGS for
  * host memory, unreachable devices or misaligned pointers.  Only D is
  * gathered; completion on every GPU means the full D is complete there.
@@ -215,6 +241,25 @@ int gemm_sm100a_generate_nvfp4(void* out_packed, void* out_scales, float scale,
  */
 int gemm_sm100a_umma_peak(int32_t dtype, int32_t cta_group, int32_t num_ctas, int32_t depth,
                           int32_t iters, unsigned long long* results, void* stream);
+
+/*
+ * TMA-2D HBM read-throughput probe (replaces the reference's
+ * tma2d_throughput/tma2d_tput.cu: kernel :42-126, launch :131-219).  Launches
+ * ctas_per_sm one-warp CTAs per SM (227 KiB of shared memory each, as the
+ * reference pins it), which stream the 32-bit words of `buf` (read as a
+ * (bytes / (4 * box_width)) x box_width row-major tensor, whole box_rows-row
+ * tiles only) through a `stages`-deep ring of (box_rows x box_width) TMA
+ * tiles.  results (device, caller-owned, 5 * num_SMs * ctas_per_sm uint64)
+ * receives per CTA {clock64 cycles, %globaltimer ns, tiles loaded, XOR of the
+ * first 32 words of every tile it loaded, status (0, or 3 if a load wait ran
+ * out after 2 s)}.  box_width: 4..256 words, a multiple of 4; box_rows 1..256;
+ * tiles of at least 128 bytes.  Time it with events on `stream` after
+ * flushing L2: bytes / time is the TMA read roof.  Returns GEMM_OK,
+ * GEMM_ERR_BAD_ARGS, GEMM_ERR_CANNOT_IMPLEMENT (ring over shared memory) or
+ * GEMM_ERR_LAUNCH; asynchronous.
+ */
+int gemm_sm100a_tma_read_probe(const void* buf, int64_t bytes, int32_t box_width, int32_t box_rows,
+                               int32_t stages, int32_t ctas_per_sm, unsigned long long* results, void* stream);
 
 #ifdef __cplusplus
 }

@@ -26,7 +26,8 @@ DTYPE_NAMES = {BF16: "BF16", FP8_E4M3: "FP8_E4M3", NVFP4: "NVFP4"}
 DTYPE_BITS = {BF16: 16, FP8_E4M3: 8, NVFP4: 4}
 
 OK, ERR_CANNOT_IMPLEMENT, ERR_LAUNCH, ERR_TIMEOUT, ERR_BAD_ARGS = 0, -1, -2, -3, -4
-FLAG_INJECT_STALL = 1
+FLAG_INJECT_STALL, FLAG_DIRECT_EPILOGUE = 1, 2
+COL_MAJOR, ROW_MAJOR = 0, 1
 
 UNIFORM, NORMAL = 0, 1
 
@@ -46,6 +47,8 @@ class GemmArgs(C.Structure):
         ("status", C.c_void_p), ("timeout_ms", C.c_uint32), ("flags", C.c_uint32),
         ("l2_prefetch", C.c_int32),
         ("clock_out", C.c_void_p),
+        ("beta", C.c_float), ("c", C.c_void_p), ("ldc", C.c_int64), ("d_layout", C.c_int32),
+        ("scale_a", C.c_float), ("scale_b", C.c_float),
     ]
 
 
@@ -57,6 +60,7 @@ class GemmInfo(C.Structure):
         ("smem_bytes_per_stage", C.c_int64), ("smem_bytes", C.c_int64),
         ("tmem_columns", C.c_int32), ("grid_ctas", C.c_int32), ("num_tiles", C.c_int64),
         ("num_sms", C.c_int32), ("can_implement", C.c_int32), ("reason", C.c_char * 128),
+        ("epilogue_staging_buffers", C.c_int32),
     ]
 
 
@@ -65,6 +69,7 @@ EXPORTED = (
     "gemm_sm100a_query", "gemm_sm100a_launch", "gemm_sm100a_launch_gather", "gemm_sm100a_read_status",
     "gemm_sm100a_strerror", "gemm_sm100a_version",
     "gemm_sm100a_generate", "gemm_sm100a_generate_nvfp4", "gemm_sm100a_umma_peak",
+    "gemm_sm100a_tma_read_probe",
 )
 
 
@@ -104,6 +109,8 @@ def lib():
         L.gemm_sm100a_generate_nvfp4.argtypes = [vp, vp, f32, u64, u64, i64, i64, i64, vp]
         L.gemm_sm100a_umma_peak.restype = C.c_int
         L.gemm_sm100a_umma_peak.argtypes = [i32, i32, i32, i32, i32, vp, vp]
+        L.gemm_sm100a_tma_read_probe.restype = C.c_int
+        L.gemm_sm100a_tma_read_probe.argtypes = [vp, i64, i32, i32, i32, i32, vp, vp]
         _lib = L
     return _lib
 
@@ -121,15 +128,19 @@ def make_args(*, dtype: int, m: int, n: int, k: int, a: int, b: int, d: int,
               tile_m: int = 0, tile_n: int = 0, tile_k: int = 0, stages: int = 0,
               cta_group: int = 0, cluster_m: int = 0, max_ctas: int = 0, raster_group: int = 0,
               status: int | None = None, timeout_ms: int = 0, flags: int = 0,
-              l2_prefetch: int = 0, clock_out: int | None = None) -> GemmArgs:
-    """GemmArgs from raw device addresses (ints).  Leading dimensions default to packed."""
+              l2_prefetch: int = 0, clock_out: int | None = None, beta: float = 0.0,
+              c: int | None = None, ldc: int | None = None, d_layout: int = 0,
+              scale_a: float = 1.0, scale_b: float = 1.0) -> GemmArgs:
+    """GemmArgs from raw device addresses (ints).  Leading dimensions default to packed
+    (ldd and ldc follow d_layout: m for column-major, n for row-major)."""
     g = GemmArgs()
     g.struct_size = C.sizeof(GemmArgs)
     g.dtype = dtype
     g.m, g.n, g.k = m, n, k
     g.a, g.lda = a, (k if lda is None else lda)
     g.b, g.ldb = b, (k if ldb is None else ldb)
-    g.d, g.ldd = d, (m if ldd is None else ldd)
+    packed_ld = m if d_layout == COL_MAJOR else n
+    g.d, g.ldd = d, (packed_ld if ldd is None else ldd)
     g.sfa, g.sfb = sfa, sfb
     g.alpha = alpha
     g.tile_m, g.tile_n, g.tile_k, g.stages = tile_m, tile_n, tile_k, stages
@@ -138,6 +149,8 @@ def make_args(*, dtype: int, m: int, n: int, k: int, a: int, b: int, d: int,
     g.timeout_ms, g.flags = timeout_ms, flags
     g.l2_prefetch = l2_prefetch
     g.clock_out = clock_out
+    g.beta, g.c, g.ldc = beta, c, (packed_ld if ldc is None else ldc)
+    g.d_layout, g.scale_a, g.scale_b = d_layout, scale_a, scale_b
     return g
 
 
@@ -220,6 +233,48 @@ def umma_peak(dtype: int, cta_group: int = 1, num_ctas: int = 1, depth: int = 25
     return {"dtype": DTYPE_NAMES[dtype], "cta_group": cta_group, "num_ctas": num_ctas, "depth": depth,
             "iters": iters, "flop_per_clk_per_sm": statistics.median(fpc), "sm_mhz": statistics.median(mhz),
             "tflops": total * len(leaders) / (max(x[1] for x in leaders) * 1e-9) / 1e12}
+
+
+L2_FLUSH_BYTES = 256 << 20     # twice the B200's 126 MB L2
+
+
+def tma_read_probe(buf, box_rows: int, stages: int, ctas_per_sm: int = 1, box_width: int = 128,
+                   flush=None, device=None) -> dict:
+    """Run the TMA-2D read probe over the device tensor `buf` once (L2 flushed first by
+    writing `flush`, a device buffer larger than L2) and summarise it: bytes / event time,
+    per-CTA cycles, tiles and cycles per TMA load -- the columns of the reference's
+    tma2d_throughput results (tma2d_tput_results.csv)."""
+    import statistics
+    import torch
+    dev = buf.device if device is None else torch.device(device)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    grid = sms * ctas_per_sm
+    res = torch.zeros(5 * grid, dtype=torch.int64, device=dev)
+    st = torch.cuda.current_stream(dev)
+    if flush is not None:
+        flush.fill_(0xA5)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nbytes = buf.numel() * buf.element_size()
+    e0.record(st)
+    rc = lib().gemm_sm100a_tma_read_probe(C.c_void_p(buf.data_ptr()), nbytes, box_width, box_rows, stages,
+                                          ctas_per_sm, C.c_void_p(res.data_ptr()), C.c_void_p(st.cuda_stream))
+    e1.record(st)
+    if rc != OK:
+        raise GemmError(rc, "gemm_sm100a_tma_read_probe")
+    e1.synchronize()
+    r = res.view(grid, 5).cpu().tolist()
+    if any(x[4] for x in r):
+        raise GemmError(ERR_TIMEOUT, "tma_read_probe wait")
+    tile_bytes = 4 * box_width * box_rows
+    tiles = sum(x[2] for x in r)
+    ms = e0.elapsed_time(e1)
+    busy = [x for x in r if x[2] > 0]
+    cyc = statistics.mean(x[0] for x in busy)
+    return {"ctas_per_sm": ctas_per_sm, "stages": stages, "box_width": box_width, "box_rows": box_rows,
+            "bytes_in_flight_per_sm": ctas_per_sm * stages * tile_bytes, "bytes": tiles * tile_bytes,
+            "ms": ms, "GBps": tiles * tile_bytes / (ms * 1e-3) / 1e9, "sm_cycles_avg": cyc,
+            "tma_ops_avg": statistics.mean(x[2] for x in busy), "cycles_per_tma": statistics.mean(x[0] / x[2] for x in busy),
+            "checksums": [x[3] for x in r], "tiles_per_cta": [x[2] for x in r]}
 
 
 def sf_bytes(rows: int, cols: int) -> int:

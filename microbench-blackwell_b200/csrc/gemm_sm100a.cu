@@ -55,6 +55,13 @@ using namespace sm100;
 #ifndef GEMM_TRACE
 #define GEMM_TRACE 0            // 1: log CTA 0's pipeline events (trace builds only)
 #endif
+#ifndef GEMM_WIDE_EPI_WARPS
+#define GEMM_WIDE_EPI_WARPS 8   // epilogue warps of a 512-column tile (8 or 16)
+#endif
+#ifndef GEMM_WIDE_EARLY_RELEASE
+#define GEMM_WIDE_EARLY_RELEASE 1  // 1: a TMEM-filling accumulator is drained into registers and released
+                                   //    before D is written; 0: written chunk by chunk, released after the last read
+#endif
 
 #if GEMM_TRACE
 // Pipeline event log of CTA 0 (trace builds only).  Each role writes its own
@@ -78,7 +85,9 @@ template <int V>
 struct IntC { static constexpr int value = V; };
 
 // Threads per CTA: producer warp + MMA warp + EPI_WARPS epilogue warps.
-__host__ __device__ constexpr int epi_warps_for(int bn) { return bn > 256 ? 8 : 4; }
+// Epilogue warps: 4 (one per TMEM lane quadrant), or GEMM_WIDE_EPI_WARPS for a
+// 512-column tile, whose single accumulator is drained into registers.
+__host__ __device__ constexpr int epi_warps_for(int bn) { return bn > 256 ? GEMM_WIDE_EPI_WARPS : 4; }
 __host__ __device__ constexpr int threads_for(int bn) { return 64 + 32 * epi_warps_for(bn); }
 constexpr int kSmemLimit = 232448;      // 227 KiB of opt-in dynamic shared memory per CTA
 constexpr int kBarrierBytes = 1024;     // barrier block + bookkeeping words
@@ -120,6 +129,13 @@ struct KernelParams {
   int32_t l2_prefetch;    // k-blocks the L2 prefetch cursor runs ahead of the loads (0 = off)
   unsigned long long* clock_out;   // optional: CTA 0's [cycles, ns] over the launch
   int32_t num_acc;        // accumulator buffers in TMEM (2 = epilogue overlaps the next tile)
+  float beta;             // D = alpha * acc + beta * C (C read only when beta != 0)
+  const __nv_bfloat16* c; // C, same layout as D, leading dimension ldc
+  int64_t ldc;
+  int32_t d_row_major;    // 0: D (and C) column-major (M contiguous), 1: row-major (N contiguous)
+  int32_t stg_bufs;       // staging buffers per epilogue group (0 = direct stores from registers)
+  uint32_t stg_offset;    // shared-memory offset of the staging area from the aligned base
+  uint32_t stg_bytes;     // bytes of one staging buffer (BM rows x CW columns of bf16)
 };
 
 // Elements of each dtype in one 128-byte swizzle atom row.
@@ -235,6 +251,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_sfa,   // NVFP4 pair kernel only
                    const __grid_constant__ CUtensorMap tmap_sfb,   // NVFP4 pair kernel only
+                   const __grid_constant__ CUtensorMap tmap_d,     // D, for the staged epilogue's TMA stores
                    const __grid_constant__ KernelParams p) {
   // A rows per CTA.  128 fills the 128 TMEM lanes; a 1-SM TILE_M = 64 tile
   // (M = 64 MMA) puts row r of the accumulator in lane 32*(r/16) + r%16, i.e.
@@ -280,6 +297,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       prefetch_tmap(&tmap_sfa);
       prefetch_tmap(&tmap_sfb);
     }
+    if (p.stg_bufs > 0) prefetch_tmap(&tmap_d);
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(full_bar + 8u * s, 1);
       mbar_init(empty_bar + 8u * s, 1);
@@ -559,9 +577,29 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     });
   } else {
     // ------------------------------------------------------------ epilogue
-    const uint32_t q = warp & 3u;                 // TMEM lane quadrant of this warp
-    constexpr int COLS = BN / (EPI_WARPS / 4);    // accumulator columns per epilogue warp
-    const int c_begin = (int)((warp - 2u) / 4u) * COLS;
+    // Warps 2..: a group of 4 warps (one per TMEM lane quadrant, 128 lanes)
+    // owns COLS accumulator columns of the tile and emits them in chunks of
+    // CW columns: tcgen05.ld -> alpha * acc (+ beta * C) -> bf16 pairs, then
+    // either staged through shared memory and written by one TMA store per
+    // chunk (every D column of the chunk is one contiguous BM-row run, whole
+    // cache lines), or stored directly from registers when the staging
+    // buffers do not fit next to the ring.
+    const uint32_t q = warp & 3u;                   // TMEM lane quadrant of this warp
+    constexpr int GROUPS = EPI_WARPS / 4;
+    constexpr int COLS = BN / GROUPS;               // accumulator columns per group
+    constexpr int CW = COLS % 32 == 0 ? 32 : 16;    // columns per chunk (one tcgen05.ld)
+    const int grp = (int)((warp - 2u) / 4u);
+    const int c_begin = grp * COLS;
+    const uint32_t gtid = ((warp - 2u) & 3u) * 32u + lane;   // thread index within the group
+    const bool issuer = gtid == 0;
+    const uint32_t bar_id = 1u + (uint32_t)grp;     // named barrier of this group
+    const int q_rows = BM / 4;                      // accumulator rows in this warp's quadrant
+    const int r_loc = q_rows * (int)q + (int)lane;  // row within the CTA's BM rows (lane < q_rows)
+    const float alpha = p.alpha, beta = p.beta;
+    const bool row_major = p.d_row_major != 0;
+    const int nbuf = p.stg_bufs;
+    const uint32_t stg_grp = base + p.stg_offset + (uint32_t)(grp * nbuf) * p.stg_bytes;
+    uint32_t chunk_no = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t leader_tempty = CG == 2 ? mapa_shared(tempty_bar, 0) : tempty_bar;
@@ -571,118 +609,192 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       int um, un;
       unit_coords(u, p, um, un);
       // Warp-uniform decision: tcgen05.ld below is warp-collective, so every
-      // lane must agree to proceed even if one lane saw an abort.
+      // lane must agree to proceed even if one lane saw an abort.  Once one
+      // warp of a group has seen the phase complete, every warp of the group
+      // does (the first probe tests the barrier before the abort flag), so
+      // the group's named barriers below never wait for a warp that left.
       const bool ok = wait_bar<false>(tfull_bar + 8u * acc, acc_phase, ctl, ROLE_EPILOGUE, acc);
       if (!__all_sync(0xffffffffu, ok)) break;
       if (warp == 2) TRACE_EVENT(3u, 1u, acc);
       tc_fence_after();
-      const int q_rows = BM / 4;                  // accumulator rows in this warp's quadrant
-      const int64_t row = (int64_t)um * MMA_M + (int64_t)cta_rank * BM + q_rows * (int)q + lane;
+      const int64_t m0 = (int64_t)um * MMA_M + (int64_t)cta_rank * BM;
+      const int64_t row = m0 + r_loc;
       const int64_t n0 = (int64_t)un * BN;
       const bool row_ok = (int)lane < q_rows && row < p.m;
-      __nv_bfloat16* const dptr = p.d + row;
       const uint32_t t_row = tmem_base + ((32u * q) << 16) + (uint32_t)(acc * BN);
-      bool released = false;
+
+      auto release_acc = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 2) mbar_arrive_cluster(leader_tempty + 8u * acc); else mbar_arrive(tempty_bar + 8u * acc);
+        }
+      };
+
+      // alpha * acc for CW columns of this thread's row, rounded to bf16 pairs.
+      auto convert = [&](const uint32_t (&r)[CW], uint32_t (&o)[CW / 2]) {
+#pragma unroll
+        for (int j = 0; j < CW; j += 2) {
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(alpha * __uint_as_float(r[j]), alpha * __uint_as_float(r[j + 1]));
+          o[j / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+      };
+      // alpha * acc + beta * C in fp32, rounded once to bf16 pairs (C in D's layout).
+      auto convert_c = [&](int c, const uint32_t (&r)[CW], uint32_t (&o)[CW / 2]) {
+        const int64_t col0 = n0 + c;
+#pragma unroll
+        for (int j = 0; j < CW; j += 2) {
+          float c0 = 0.f, c1 = 0.f;
+          if (row_ok) {
+            if (!row_major) {
+              if (col0 + j < p.n) c0 = __bfloat162float(p.c[(col0 + j) * p.ldc + row]);
+              if (col0 + j + 1 < p.n) c1 = __bfloat162float(p.c[(col0 + j + 1) * p.ldc + row]);
+            } else {
+              const __nv_bfloat16* crow = p.c + row * p.ldc + col0;
+              if (col0 + j < p.n) c0 = __bfloat162float(crow[j]);
+              if (col0 + j + 1 < p.n) c1 = __bfloat162float(crow[j + 1]);
+            }
+          }
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaf(beta, c0, alpha * __uint_as_float(r[j])),
+                                                         fmaf(beta, c1, alpha * __uint_as_float(r[j + 1])));
+          o[j / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+      };
+
+      // Write CW columns (tile column offset c) of this thread's row.
+      auto emit = [&](int c, const uint32_t (&o)[CW / 2]) {
+        const int64_t col0 = n0 + c;
+        if (nbuf > 0) {
+          const uint32_t buf = stg_grp + (nbuf == 2 ? (chunk_no & 1u) : 0u) * p.stg_bytes;
+          // The TMA store that last read this buffer must be done reading it.
+          if (issuer) {
+            if (nbuf == 2) bulk_wait_group_read<1>(); else bulk_wait_group_read<0>();
+          }
+          named_bar_sync(bar_id, 128);
+          if ((int)lane < q_rows) {
+            if (!row_major) {
+              // [CW columns][BM rows]: each store instruction fills one column's 64-byte run.
+#pragma unroll
+              for (int j = 0; j < CW; ++j)
+                st_shared_u16(buf + (uint32_t)((j * BM + r_loc) * 2), (uint16_t)(j % 2 == 0 ? (o[j / 2] & 0xFFFFu) : (o[j / 2] >> 16)));
+            } else {
+              // [BM rows][CW columns] in the 64-byte (CW 32) or 32-byte (CW 16) TMA swizzle:
+              // 16-byte vector v of row r sits at vector v ^ ((r >> 1) & 3) (CW 32) or
+              // v ^ ((r >> 2) & 1) (CW 16), which spreads a warp's rows over all banks.
+              const uint32_t rbase = buf + (uint32_t)(r_loc * CW * 2);
+              const uint32_t sw = CW == 32 ? (((uint32_t)r_loc >> 1) & 3u) : (((uint32_t)r_loc >> 2) & 1u);
+#pragma unroll
+              for (int v = 0; v < CW / 8; ++v)
+                st_shared_v4(rbase + (((uint32_t)v ^ sw) << 4), o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+            }
+          }
+          fence_proxy_async_shared();
+          named_bar_sync(bar_id, 128);
+          if (issuer) {
+            if (!row_major) tma_store_2d(&tmap_d, buf, (int32_t)m0, (int32_t)col0);
+            else tma_store_2d(&tmap_d, buf, (int32_t)col0, (int32_t)m0);
+            bulk_commit_group();
+          }
+          if (p.n_d_peer > 0) {
+            // Fused gather (column-major D only): the staged block again, as 16-byte
+            // stores of 8 rows each, into every peer destination.
+            const int vpc = BM / 8;
+            for (int v = (int)gtid; v < CW * vpc; v += 128) {
+              const int j = v / vpc, r8 = (v - j * vpc) * 8;
+              const int64_t col = col0 + j, rr = m0 + r8;
+              if (col >= p.n || rr >= p.m) continue;
+              const uint4 val = ld_shared_v4(buf + (uint32_t)((j * BM + r8) * 2));
+              for (int gp = 0; gp < p.n_d_peer; ++gp) {
+                __nv_bfloat16* dst = p.d_peer[gp] + col * p.ldd + rr;
+                if (rr + 8 <= p.m) {
+                  *reinterpret_cast<uint4*>(dst) = val;
+                } else {
+                  const uint32_t wv[4] = {val.x, val.y, val.z, val.w};
+                  uint16_t* d16 = reinterpret_cast<uint16_t*>(dst);
+                  for (int e = 0; e < (int)(p.m - rr); ++e)
+                    d16[e] = (uint16_t)(e % 2 == 0 ? (wv[e / 2] & 0xFFFFu) : (wv[e / 2] >> 16));
+                }
+              }
+            }
+          }
+          ++chunk_no;
+        } else if (row_ok) {
+          if (!row_major) {
+            uint16_t* dst = reinterpret_cast<uint16_t*>(p.d + row) + col0 * p.ldd;
+#pragma unroll
+            for (int j = 0; j < CW; ++j)
+              if (col0 + j < p.n) dst[j * p.ldd] = (uint16_t)(j % 2 == 0 ? (o[j / 2] & 0xFFFFu) : (o[j / 2] >> 16));
+            for (int gp = 0; gp < p.n_d_peer; ++gp) {   // fused gather: the same block into each peer D
+              uint16_t* pdst = reinterpret_cast<uint16_t*>(p.d_peer[gp] + row) + col0 * p.ldd;
+#pragma unroll
+              for (int j = 0; j < CW; ++j)
+                if (col0 + j < p.n) pdst[j * p.ldd] = (uint16_t)(j % 2 == 0 ? (o[j / 2] & 0xFFFFu) : (o[j / 2] >> 16));
+            }
+          } else {
+            __nv_bfloat16* drow = p.d + row * p.ldd + col0;
+#pragma unroll
+            for (int v = 0; v < CW / 8; ++v) {
+              if (col0 + 8 * v + 8 <= p.n) {
+                *reinterpret_cast<uint4*>(drow + 8 * v) = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+              } else {
+                uint16_t* d16 = reinterpret_cast<uint16_t*>(drow);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  if (col0 + 8 * v + e < p.n)
+                    d16[8 * v + e] = (uint16_t)(e % 2 == 0 ? (o[4 * v + e / 2] & 0xFFFFu) : (o[4 * v + e / 2] >> 16));
+              }
+            }
+          }
+        }
+      };
+
+      auto tmem_chunk = [&](uint32_t taddr, uint32_t (&r)[CW]) {
+        if constexpr (CW == 32) tmem_ld32(taddr, r); else tmem_ld16(taddr, r);
+        tmem_ld_wait();
+      };
+
       if constexpr (COLS % 32 == 0) {
-        if (p.num_acc == 1) {
+        if (GEMM_WIDE_EARLY_RELEASE && p.num_acc == 1 && beta == 0.f) {
           // Single accumulator (the tile fills TMEM): drain it into registers
           // as packed bf16 pairs, release it at once so the next tile's MMAs
           // start, then write D while that mainloop runs.
           uint32_t pk[COLS / 2];
 #pragma unroll
           for (int cc = 0; cc < COLS; cc += 32) {
-            uint32_t r[32];
-            tmem_ld32(t_row + (uint32_t)(c_begin + cc), r);
-            tmem_ld_wait();
+            uint32_t r[32], o[16];
+            tmem_chunk(t_row + (uint32_t)(c_begin + cc), r);
+            convert(r, o);
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const __nv_bfloat162 h2 = __floats2bfloat162_rn(p.alpha * __uint_as_float(r[j]),
-                                                             p.alpha * __uint_as_float(r[j + 1]));
-              pk[(cc + j) / 2] = *reinterpret_cast<const uint32_t*>(&h2);
-            }
+            for (int j = 0; j < 16; ++j) pk[cc / 2 + j] = o[j];
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if constexpr (CG == 2) mbar_arrive_cluster(leader_tempty + 8u * acc); else mbar_arrive(tempty_bar + 8u * acc);
+          release_acc();
+#pragma unroll
+          for (int cc = 0; cc < COLS; cc += 32) {
+            uint32_t o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = pk[cc / 2 + j];
+            emit(c_begin + cc, o);
           }
-          released = true;
-          if (row_ok) {
-            const int64_t col0 = n0 + c_begin;
-            const int64_t left = (int64_t)p.n - col0;
-            const int n_valid = left < (int64_t)COLS ? (int)left : COLS;   // columns inside D
-            uint16_t* dst = reinterpret_cast<uint16_t*>(dptr) + col0 * p.ldd;
-            const int64_t step = p.ldd;
-#pragma unroll
-            for (int j = 0; j < COLS; ++j) {
-              if (j < n_valid) *dst = (uint16_t)(j % 2 == 0 ? (pk[j / 2] & 0xFFFFu) : (pk[j / 2] >> 16));
-              dst += step;
-            }
-            for (int gp = 0; gp < p.n_d_peer; ++gp) {   // fused gather: the same block into each peer D
-              uint16_t* pdst = reinterpret_cast<uint16_t*>(p.d_peer[gp] + row) + col0 * p.ldd;
-#pragma unroll
-              for (int j = 0; j < COLS; ++j) {
-                if (j < n_valid) *pdst = (uint16_t)(j % 2 == 0 ? (pk[j / 2] & 0xFFFFu) : (pk[j / 2] >> 16));
-                pdst += step;
-              }
-            }
-          }
-        } else {
-#pragma unroll 1
-          for (int c = c_begin; c < c_begin + COLS; c += 32) {
-            uint32_t r[32];
-            tmem_ld32(t_row + (uint32_t)c, r);
-            tmem_ld_wait();
-            if (row_ok) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int64_t col = n0 + c + j;
-                if (col < p.n) dptr[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
-              }
-              for (int gp = 0; gp < p.n_d_peer; ++gp) {
-                __nv_bfloat16* const pp = p.d_peer[gp] + row;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  const int64_t col = n0 + c + j;
-                  if (col < p.n) pp[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
-                }
-              }
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = c_begin; c < c_begin + COLS; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(t_row + (uint32_t)c, r);
-          tmem_ld_wait();
-          if (row_ok) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int64_t col = n0 + c + j;
-              if (col < p.n) dptr[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
-            }
-            for (int gp = 0; gp < p.n_d_peer; ++gp) {
-              __nv_bfloat16* const pp = p.d_peer[gp] + row;
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int64_t col = n0 + c + j;
-                if (col < p.n) pp[col * p.ldd] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
-              }
-            }
-          }
+          if (warp == 2) TRACE_EVENT(3u, 2u, acc);
+          if (++acc == p.num_acc) { acc = 0; acc_phase ^= 1u; }
+          continue;
         }
       }
-      if (!released) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if constexpr (CG == 2) mbar_arrive_cluster(leader_tempty + 8u * acc); else mbar_arrive(tempty_bar + 8u * acc);
-        }
+      // Chunk by chunk: the accumulator is released right after its last
+      // chunk has been read from TMEM, before that chunk is written out.
+#pragma unroll 1
+      for (int cc = 0; cc < COLS; cc += CW) {
+        uint32_t r[CW], o[CW / 2];
+        tmem_chunk(t_row + (uint32_t)(c_begin + cc), r);
+        if (cc + CW == COLS) release_acc();
+        if (beta != 0.f) convert_c(c_begin + cc, r, o); else convert(r, o);
+        emit(c_begin + cc, o);
       }
       if (warp == 2) TRACE_EVENT(3u, 2u, acc);
       if (++acc == p.num_acc) { acc = 0; acc_phase ^= 1u; }
     }
+    // Every TMA store of this group must have completed before the CTA exits.
+    if (issuer && nbuf > 0) bulk_wait_group<0>();
   }
 
   // ------------------------------------------------------------ teardown
@@ -722,6 +834,9 @@ struct Resolved {
   int64_t smem_bytes;
   int tmem_cols, num_acc, threads, sf_slots;
   uint32_t row_bytes;
+  int cw, stg_bufs;                 // epilogue chunk width; staging buffers per group (0 = direct stores)
+  uint32_t stg_bytes, stg_offset;
+  float alpha_eff;                  // alpha * scale_a * scale_b
   int num_m_units, num_n_units, num_units, num_k_blocks;
   int grid, num_sms, raster_group;
   char reason[128];
@@ -788,7 +903,16 @@ int resolve(const GemmArgs* a, Resolved& r) {
   // Element size in bytes (NVFP4: half a byte) and alignment (128-bit, as the reference's Alignment{A,B,D}).
   const int64_t bits = r.dt == 0 ? 16 : (r.dt == 1 ? 8 : 4);
   if (a->lda < a->k || a->ldb < a->k) FAIL("lda/ldb must be >= k");
-  if (a->ldd < a->m) FAIL("ldd must be >= m");
+  if (a->d_layout != GEMM_LAYOUT_COL_MAJOR && a->d_layout != GEMM_LAYOUT_ROW_MAJOR) FAIL("unknown d_layout %d", a->d_layout);
+  const bool d_rm = a->d_layout == GEMM_LAYOUT_ROW_MAJOR;
+  if (a->ldd < (d_rm ? a->n : a->m)) FAIL("ldd must be >= %s", d_rm ? "n (row-major D)" : "m");
+  if (a->beta != 0.f) {
+    if (!a->c) { snprintf(r.reason, sizeof(r.reason), "beta != 0 needs C"); return GEMM_ERR_BAD_ARGS; }
+    if (a->ldc < (d_rm ? a->n : a->m)) FAIL("ldc must be >= %s", d_rm ? "n (row-major C)" : "m");
+    if ((a->ldc * 16) % 128 != 0) FAIL("ldc must be a multiple of 8");
+    if ((uintptr_t)a->c & 15) FAIL("C must be 16-byte aligned");
+  }
+  r.alpha_eff = a->alpha * (a->scale_a != 0.f ? a->scale_a : 1.f) * (a->scale_b != 0.f ? a->scale_b : 1.f);
   if ((a->lda * bits) % 128 != 0 || (a->ldb * bits) % 128 != 0) FAIL("lda/ldb rows must be 16-byte multiples");
   if ((a->ldd * 16) % 128 != 0) FAIL("ldd must be a multiple of 8");
   if (((uintptr_t)a->a | (uintptr_t)a->b | (uintptr_t)a->d) & 15) FAIL("A/B/D must be 16-byte aligned");
@@ -816,6 +940,22 @@ int resolve(const GemmArgs* a, Resolved& r) {
   if (r.stages < 1) FAIL("stages must be >= 1");
   if (r.stages > r.max_stages) FAIL("stages %d exceed shared memory (max %d at %u B/stage)", r.stages, r.max_stages, r.stage_bytes);
   r.smem_bytes = fixed + (int64_t)r.stages * r.stage_bytes;
+  // Epilogue staging: per group of 4 epilogue warps, one or two buffers of
+  // (rows per CTA) x CW bf16 after the ring and barriers, when they fit; else
+  // the epilogue stores D directly from registers.  The stage count (and so
+  // can_implement) never depends on it.
+  {
+    const int groups = epi_warps_for(r.bn) / 4;
+    r.cw = (r.bn / groups) % 32 == 0 ? 32 : 16;
+    r.stg_bytes = (uint32_t)((r.bm / r.cg) * r.cw * 2);
+    const int64_t ring_end = ((int64_t)r.stages * r.stage_bytes + kBarrierBytes + 1023) / 1024 * 1024;
+    r.stg_offset = (uint32_t)ring_end;
+    r.stg_bufs = 0;
+    if (!(a->flags & GEMM_FLAG_DIRECT_EPILOGUE))
+      for (int nb = 2; nb >= 1 && r.stg_bufs == 0; --nb)
+        if (1024 + ring_end + (int64_t)groups * nb * r.stg_bytes <= kSmemLimit) r.stg_bufs = nb;
+    if (r.stg_bufs > 0) r.smem_bytes = 1024 + ring_end + (int64_t)groups * r.stg_bufs * r.stg_bytes;
+  }
   // One CTA per SM: the persistent schedule assumes it, and a second resident
   // CTA would only stall in tcgen05.alloc until the first frees its columns.
   if (r.smem_bytes < kMinSmemPerCta) r.smem_bytes = kMinSmemPerCta;
@@ -866,7 +1006,8 @@ int resolve(const GemmArgs* a, Resolved& r) {
 bool encode_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType t, uint64_t inner, uint64_t outer,
                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, uint32_t swizzle_bytes) {
   const CUtensorMapSwizzle swz = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                               : (swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+                               : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                               : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
@@ -891,7 +1032,7 @@ bool encode_sf_3d(CUtensorMap* m, const void* ptr, uint64_t kblocks, uint64_t ro
   return res == CUDA_SUCCESS;
 }
 
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, KernelParams);
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, KernelParams);
 
 template <int DT, int CG, int BN>
 KernelFn kernel_ptr() { return gemm_sm100a_kernel<DT, CG, BN>; }
@@ -947,6 +1088,7 @@ extern "C" int gemm_sm100a_query(const GemmArgs* args, GemmInfo* info) {
     info->tmem_columns = r.tmem_cols; info->grid_ctas = r.grid; info->num_tiles = r.num_units;
     info->num_sms = r.num_sms; info->can_implement = rc == GEMM_OK;
     memcpy(info->reason, r.reason, sizeof(info->reason));
+    info->epilogue_staging_buffers = r.stg_bufs;
   }
   return rc;
 }
@@ -988,6 +1130,21 @@ static int launch_impl(const GemmArgs* args, void* const* peers, int n_peers, vo
       return GEMM_ERR_CANNOT_IMPLEMENT;
   }
 
+  // D for the staged epilogue's TMA stores: box = the CTA's rows x one CW-column
+  // chunk; column-major unswizzled, row-major in the 64- / 32-byte swizzle the
+  // epilogue writes its staging rows in.
+  CUtensorMap tm_d;
+  memset(&tm_d, 0, sizeof(tm_d));
+  if (r.stg_bufs > 0) {
+    const bool d_rm = a.d_layout == GEMM_LAYOUT_ROW_MAJOR;
+    const uint32_t rows = (uint32_t)(r.bm / r.cg);
+    const bool okd = d_rm ? encode_2d(&tm_d, a.d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)a.n, (uint64_t)a.m,
+                                      (uint64_t)a.ldd * 2u, (uint32_t)r.cw, rows, r.cw == 32 ? 64u : 32u)
+                          : encode_2d(&tm_d, a.d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)a.m, (uint64_t)a.n,
+                                      (uint64_t)a.ldd * 2u, rows, (uint32_t)r.cw, 0u);
+    if (!okd) return GEMM_ERR_CANNOT_IMPLEMENT;
+  }
+
   KernelParams p;
   memset(&p, 0, sizeof(p));
   p.m = (int32_t)a.m; p.n = (int32_t)a.n; p.k = (int32_t)a.k;
@@ -1000,7 +1157,14 @@ static int launch_impl(const GemmArgs* args, void* const* peers, int n_peers, vo
   p.sf_stage_bytes = r.sf_stage_bytes;
   p.idesc = make_idesc(r.dt, r.bm, r.bn > 256 ? 256 : r.bn);
   p.num_acc = r.num_acc;
-  p.alpha = a.alpha;
+  p.alpha = r.alpha_eff;
+  p.beta = a.beta;
+  p.c = reinterpret_cast<const __nv_bfloat16*>(a.c);
+  p.ldc = a.ldc;
+  p.d_row_major = a.d_layout == GEMM_LAYOUT_ROW_MAJOR ? 1 : 0;
+  p.stg_bufs = r.stg_bufs;
+  p.stg_offset = r.stg_offset;
+  p.stg_bytes = r.stg_bytes;
   p.d = reinterpret_cast<__nv_bfloat16*>(a.d);
   p.ldd = a.ldd;
   p.status = a.status;
@@ -1035,7 +1199,7 @@ static int launch_impl(const GemmArgs* args, void* const* peers, int n_peers, vo
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tma_a, tmb_b, tm_sfa, tm_sfb, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, tma_a, tmb_b, tm_sfa, tm_sfb, tm_d, p);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return GEMM_ERR_LAUNCH;
@@ -1080,6 +1244,8 @@ bool block_inside_allocation(const void* ptr, size_t bytes, int owner, int curre
 extern "C" int gemm_sm100a_launch_gather(const GemmArgs* args, void* const* peer_d, int32_t n_peers,
                                          void* stream) {
   if (n_peers < 0 || n_peers > kMaxGatherPeers || (n_peers > 0 && !peer_d)) return GEMM_ERR_BAD_ARGS;
+  if (args && args->struct_size == sizeof(GemmArgs) && n_peers > 0 && args->d_layout != GEMM_LAYOUT_COL_MAJOR)
+    return GEMM_ERR_CANNOT_IMPLEMENT;   // the gather writes column-major D blocks
   StreamDeviceGuard guard(reinterpret_cast<cudaStream_t>(stream));
   if (!guard.ok) return GEMM_ERR_LAUNCH;
   int dev = 0;
@@ -1152,7 +1318,7 @@ extern "C" const char* gemm_sm100a_strerror(int code) {
   return "unknown error";
 }
 
-extern "C" int gemm_sm100a_version(void) { return 100; }
+extern "C" int gemm_sm100a_version(void) { return 200; }
 
 #if GEMM_TRACE
 // Trace builds only: copy CTA 0's event log (4 regions of 16384 entries, one

@@ -164,3 +164,35 @@ def test_gather_rejects_bad_destination_lists_before_any_cuda_call(pkg):
     assert L.gemm_sm100a_launch_gather(C.byref(args), arr, 8, None) == pkg.ERR_BAD_ARGS
     assert L.gemm_sm100a_launch_gather(C.byref(args), None, 1, None) == pkg.ERR_BAD_ARGS
     assert L.gemm_sm100a_launch_gather(C.byref(args), arr, -1, None) == pkg.ERR_BAD_ARGS
+
+
+def test_epilogue_staging_buffers(pkg):
+    """The TMA-store epilogue stages D in shared memory when it fits next to the
+    ring (the stage count, and so can_implement, never depends on it)."""
+    cases = [(dict(tile_n=256, tile_k=64, stages=4), 2),                       # bf16 128x256x64 S4
+             (dict(tile_n=512, tile_k=64, cta_group=2), 2),                    # pair 256x512, two groups
+             (dict(tile_n=128, tile_k=64), 0),                                 # 7 stages fill shared memory
+             (dict(tile_n=256, tile_k=64, stages=4, flags=pkg.FLAG_DIRECT_EPILOGUE), 0)]
+    for knobs, bufs in cases:
+        rc, info = pkg.query(_args(pkg, **knobs))
+        assert rc == pkg.OK and info.epilogue_staging_buffers == bufs, (knobs, info.epilogue_staging_buffers)
+        assert info.smem_bytes <= 232448
+    rc, info = pkg.query(_args(pkg, tile_n=128, tile_k=64))
+    assert info.stages == 7                                                     # as the reference's auto count
+    rc, info = pkg.query(_args(pkg, dtype=pkg.NVFP4, sfa=0x4000, sfb=0x5000, tile_n=256, tile_k=256))
+    assert rc == pkg.OK and info.stages == 4 and info.epilogue_staging_buffers == 1
+
+
+def test_epilogue_argument_checks(pkg):
+    rc, info = pkg.query(_args(pkg, beta=1.0))                                  # beta without C
+    assert rc == pkg.ERR_BAD_ARGS and b"needs C" in info.reason
+    rc, _ = pkg.query(_args(pkg, beta=1.0, c=0x6000))
+    assert rc == pkg.OK
+    rc, info = pkg.query(_args(pkg, beta=1.0, c=0x6008))                        # misaligned C
+    assert rc == pkg.ERR_CANNOT_IMPLEMENT
+    rc, info = pkg.query(_args(pkg, d_layout=2))
+    assert rc == pkg.ERR_CANNOT_IMPLEMENT and b"d_layout" in info.reason
+    rc, _ = pkg.query(_args(pkg, m=8192, n=1000, d_layout=pkg.ROW_MAJOR))       # ldd = n = 1000
+    assert rc == pkg.OK
+    rc, info = pkg.query(_args(pkg, m=1000, n=8192, d_layout=pkg.ROW_MAJOR, ldd=1000))   # ldd < n
+    assert rc == pkg.ERR_CANNOT_IMPLEMENT

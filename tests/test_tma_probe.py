@@ -1,0 +1,49 @@
+"""TMA-2D HBM read probe (the reference's tma2d_throughput/tma2d_tput.cu as a
+library entry point): every CTA must load exactly its tiles, which the XOR of
+each tile's first 32 words proves against a host computation, and the event-
+timed bandwidth must be that of HBM, not of L2 (the buffer is flushed first)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+
+def test_probe_rejects_bad_shapes_without_a_gpu(pkg):
+    L = pkg.lib()
+    f = L.gemm_sm100a_tma_read_probe
+    buf, res = C.c_void_p(0x10000), C.c_void_p(0x20000)
+    assert f(None, 1 << 20, 128, 8, 2, 1, res, None) == pkg.ERR_BAD_ARGS
+    assert f(buf, 1 << 20, 130, 8, 2, 1, res, None) == pkg.ERR_BAD_ARGS           # width not a multiple of 4
+    assert f(buf, 1 << 20, 128, 300, 2, 1, res, None) == pkg.ERR_BAD_ARGS         # box taller than 256
+    assert f(buf, 1 << 20, 4, 1, 2, 1, res, None) == pkg.ERR_BAD_ARGS             # 16-byte tiles
+    assert f(buf, 1 << 20, 128, 256, 2, 1, res, None) == pkg.ERR_CANNOT_IMPLEMENT  # 2 x 128 KiB ring
+    assert f(C.c_void_p(0x10008), 1 << 20, 128, 8, 2, 1, res, None) == pkg.ERR_BAD_ARGS
+
+
+def expected_checksums(buf, tile_words, grid):
+    """Per CTA: XOR of the first 32 words of every tile it loads (tiles b, b + grid, ...)."""
+    import torch
+    tiles = buf.numel() // tile_words
+    heads = buf[: tiles * tile_words].view(tiles, tile_words)[:, :32].cpu().numpy().view(np.uint32)
+    per_tile = np.bitwise_xor.reduce(heads, axis=1)
+    padded = np.zeros(-(-tiles // grid) * grid, dtype=np.uint32)
+    padded[:tiles] = per_tile
+    return [int(v) for v in np.bitwise_xor.reduce(padded.reshape(-1, grid), axis=0)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("box_rows,stages,ctas", [(1, 4, 1), (16, 2, 1), (64, 4, 1), (256, 1, 1), (32, 2, 2)])
+def test_probe_loads_every_tile_and_reaches_hbm_speed(pkg, cuda, box_rows, stages, ctas):
+    import torch
+    nbytes = 256 << 20                                      # twice the L2
+    g = torch.Generator(device=cuda).manual_seed(box_rows * 10 + stages)
+    buf = torch.randint(-(2 ** 31), 2 ** 31 - 1, (nbytes // 4,), dtype=torch.int32, device=cuda, generator=g)
+    flush = torch.empty(pkg.L2_FLUSH_BYTES, dtype=torch.uint8, device=cuda)
+    r = pkg.tma_read_probe(buf, box_rows=box_rows, stages=stages, ctas_per_sm=ctas, flush=flush)
+    tile_words = 128 * box_rows
+    grid = len(r["checksums"])
+    assert sum(r["tiles_per_cta"]) == buf.numel() // tile_words
+    assert r["checksums"] == expected_checksums(buf, tile_words, grid)
+    assert r["GBps"] > 200.0
+    if box_rows * stages >= 64:
+        assert r["GBps"] > 3000.0, r        # deep enough in flight to run near HBM speed
