@@ -1,14 +1,20 @@
 #!/usr/bin/env python3
 """Benchmark driver: GEMM TFLOPS and % of the measured UMMA dense peak on B200.
 
-Default workload (the metric's configuration): bf16 GEMM
-M = N = K = 8192, A row-major, B N x K, D column-major bf16, seeded
-uniform[-1,1) inputs, fp32 accumulation, 1-SM tcgen05 tile 128x256x64 with
-the deepest stage count that fits (4).  One step = one GEMM (one launch of the
-library kernel through the C ABI).  At N GPUs the GEMM is N-split with a
-fixed 8192-column slab per GPU (A replicated, B and D column-sliced, no
-collective on the data path): weak scaling, value = total FLOPs / max-over-
-ranks time.
+Default workload (BASELINE config 2's problem, the metric's configuration): bf16
+GEMM M = N = K = 8192, A row-major, B N x K, D column-major bf16, seeded
+uniform[-1,1) inputs, fp32 accumulation, CTA-pair (cta_group::2) 256x256x64
+tiles, tile groups of 4 M-tiles.  One step = one GEMM (one launch of the library
+kernel through the C ABI).  At N GPUs the GEMM is N-split with a fixed
+8192-column slab per GPU (A replicated, B and D column-sliced, no collective on
+the data path): weak scaling, value = total FLOPs / max-over-ranks time.
+
+Beside the headline the line carries: the other BASELINE configurations (3-5,
+fp8 at 8192^3, config 5 strong-scaled over the ranks with its all-gather and the
+fused GEMM+gather timed separately), config 2 exactly as stated (the 1-SM
+128x256x64 tile, stages 2..8), config 1 against the measured TMA/HBM read roof,
+the reference's CUTLASS kernel family on the same operands, the reference's
+single-CTA experiment, and the CPU baseline.
 
 ``--impl reference`` times the CPU path the reference lacks and the benchmark
 plan names as its stand-in: the OpenMP fp32-accumulate host GEMM of oracle/
@@ -38,26 +44,67 @@ DENSE_RATE_VS_BF16 = {"bf16": 1.0, "e4m3": 2.0, "nvfp4": 4.0}     # tcgen05 dens
 REF_SINGLE_CTA_TFLOPS = {"bf16": 10.4596, "e4m3": 20.6377}  # cutlass_gemm_mainloop/results.csv:461,938
 
 WORKLOADS = {
-    # name: dtype, M, N (per GPU), K, knobs, inputs
+    # name: dtype, M, N (per GPU), K, knobs, inputs.  Knobs are the fastest measured on
+    # B200 under the power cap (interleaved with CUTLASS's 2SM kernel, medians).
     "bf16_8192": dict(dtype="bf16", m=8192, n=8192, k=8192,
-                      knobs=dict(tile_n=512, tile_k=64, stages=0, cta_group=2, raster_group=1),
+                      knobs=dict(tile_n=256, tile_k=64, stages=0, cta_group=2, raster_group=4),
                       a=("uniform", 1.0), b=("uniform", 1.0), config=2),
     "bf16_8192_1sm": dict(dtype="bf16", m=8192, n=8192, k=8192,
                           knobs=dict(tile_n=256, tile_k=64, stages=4, cta_group=1, raster_group=1),
                           a=("uniform", 1.0), b=("uniform", 1.0), config=2),
     "e4m3_16384_2sm": dict(dtype="e4m3", m=16384, n=16384, k=16384,
-                           knobs=dict(tile_n=512, tile_k=128, stages=0, cta_group=2, raster_group=16),
+                           knobs=dict(tile_n=256, tile_k=128, stages=0, cta_group=2, raster_group=4),
                            a=("normal", 0.25), b=("normal", 0.25), config=3),
+    "e4m3_8192": dict(dtype="e4m3", m=8192, n=8192, k=8192,
+                      knobs=dict(tile_n=256, tile_k=128, stages=0, cta_group=2, raster_group=4),
+                      a=("normal", 0.25), b=("normal", 0.25), config=3),
     "nvfp4_mlp": dict(dtype="nvfp4", m=8192, n=28672, k=8192,
-                      knobs=dict(tile_n=256, tile_k=256, stages=0, cta_group=1, raster_group=-16),
+                      knobs=dict(tile_n=256, tile_k=256, stages=0, cta_group=2, raster_group=-16),
                       a=("normal", 1.0), b=("normal", 1.0), config=4),
+    # config 5: N is the whole problem's (57344); bench.py splits it over the ranks (strong scaling)
     "e4m3_nsplit": dict(dtype="e4m3", m=16384, n=57344, k=8192,
-                        knobs=dict(tile_n=512, tile_k=128, stages=0, cta_group=2, raster_group=16),
-                        a=("normal", 0.25), b=("normal", 0.02), config=5),
+                        knobs=dict(tile_n=256, tile_k=128, stages=0, cta_group=2, raster_group=4),
+                        a=("normal", 0.25), b=("normal", 0.02), config=5, split="strong"),
     "bf16_256": dict(dtype="bf16", m=256, n=256, k=256,
                      knobs=dict(tile_n=256, tile_k=64, stages=4, cta_group=1),
                      a=("uniform", 1.0), b=("uniform", 1.0), config=1),
 }
+
+
+def interleaved(stream, fns: dict, flop: float, rounds: int = 6, burst_s: float = 0.02, settle_s: float = 0.3):
+    """Time callables (each enqueues one launch on `stream`) in alternating bursts of about
+    burst_s, after a settle, so all see the same power-capped clock state.  Returns per name
+    the median TFLOP/s and, against the first name, the median of the per-round ratios."""
+    import torch
+    names = list(fns)
+    t0 = time.perf_counter()
+    n_settle = 0
+    while time.perf_counter() - t0 < settle_s or n_settle < 3:
+        for f in fns.values():
+            if f() != 0:
+                return None
+        stream.synchronize()
+        n_settle += 1
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for f in fns.values():
+        f()
+    e1.record(stream)
+    e1.synchronize()
+    reps = max(2, int(burst_s * 1e3 / max(e0.elapsed_time(e1) / len(fns), 1e-3)))
+    res = {k: [] for k in names}
+    for _ in range(rounds):
+        for k in names:
+            e0.record(stream)
+            for _ in range(reps):
+                fns[k]()
+            e1.record(stream)
+            e1.synchronize()
+            res[k].append(flop / (e0.elapsed_time(e1) / reps * 1e-3) / 1e12)
+    first = names[0]
+    return {k: {"tflops": statistics.median(v),
+                "ratio_to_" + first: statistics.median(a / b for a, b in zip(v, res[first]))}
+            for k, v in res.items()} | {"_rounds": rounds, "_launches_per_burst": reps}
 
 
 def load_pkg():
@@ -269,8 +316,10 @@ def effective_knobs(wl, args) -> dict:
 
 
 def config_block(wl, world, args):
+    strong = wl.get("split") == "strong"
     return {"workload": args.workload, "baseline_config": wl["config"],
-            "m": wl["m"], "n_per_gpu": wl["n"], "n_total": wl["n"] * world, "k": wl["k"],
+            "m": wl["m"], "n_per_gpu": wl["n"] // world if strong else wl["n"],
+            "n_total": wl["n"] if strong else wl["n"] * world, "k": wl["k"],
             "dtype": wl["dtype"], **effective_knobs(wl, args),
             "parallelism": f"nsplit{world}" if world > 1 else "single",
             "layout": "A row-major MxK, B NxK (K-major), D column-major bf16",
@@ -279,6 +328,32 @@ def config_block(wl, world, args):
 
 
 # ------------------------------------------------------------------ our arm
+def slab_for(wl, knobs, world, rank):
+    """N-split slab of this rank: strong-scaled workloads split their own N over the ranks,
+    the others give every rank a slab of the per-GPU N (weak scaling)."""
+    from microbench_blackwell_b200 import nsplit
+    n_total = wl["n"] if wl.get("split") == "strong" else wl["n"] * world
+    return nsplit.partition(n_total, world, rank, align=knobs.get("tile_n", 256))
+
+
+def make_gemm(pkg, wl, knobs, slab, dev, stream, seed):
+    import torch
+    dt = dtype_code(pkg, wl["dtype"])
+    with torch.cuda.stream(stream):
+        ops = pkg.make_operands(dt, wl["m"], slab.n_local, wl["k"], seed=seed,
+                                a_dist=dist_code(pkg, wl["a"][0]), a_scale=wl["a"][1],
+                                b_dist=dist_code(pkg, wl["b"][0]), b_scale=wl["b"][1],
+                                n0=slab.n0, device=dev, stream=stream.cuda_stream)
+    clock_buf = torch.zeros(2, dtype=torch.int64, device=dev)     # CTA 0's [cycles, ns] per launch
+    g = pkg.make_args(dtype=dt, m=ops.m, n=ops.n, k=ops.k, a=ops.a.data_ptr(), b=ops.b.data_ptr(),
+                      d=ops.d.data_ptr(), sfa=None if ops.sfa is None else ops.sfa.data_ptr(),
+                      sfb=None if ops.sfb is None else ops.sfb.data_ptr(), clock_out=clock_buf.data_ptr(), **knobs)
+    rc, info = pkg.query(g)
+    if rc != pkg.OK:
+        raise SystemExit(f"cannot implement: {info.reason.decode()}")
+    return ops, g, clock_buf, info
+
+
 def run_ours(args, wl, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -287,26 +362,12 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(dev)
     stream = torch.cuda.Stream(dev)
     st = stream.cuda_stream
-    dt = dtype_code(pkg, wl["dtype"])
-    m, n, k = wl["m"], wl["n"], wl["k"]
     knobs = effective_knobs(wl, args)
-    from microbench_blackwell_b200 import nsplit
-    slab = nsplit.partition(n * world, world, rank, align=knobs.get("tile_n", 256))
-    n0 = slab.n0
-    with torch.cuda.stream(stream):
-        ops = pkg.make_operands(dt, m, n, k, seed=args.seed,
-                                a_dist=dist_code(pkg, wl["a"][0]), a_scale=wl["a"][1],
-                                b_dist=dist_code(pkg, wl["b"][0]), b_scale=wl["b"][1],
-                                n0=n0, device=dev, stream=st)
+    slab = slab_for(wl, knobs, world, rank)
+    ops, gargs, clock_buf, info = make_gemm(pkg, wl, knobs, slab, dev, stream, args.seed)
+    m, n, k = ops.m, ops.n, ops.k
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    clock_buf = torch.zeros(2, dtype=torch.int64, device=dev)     # CTA 0's [cycles, ns] per launch
-    gargs = pkg.make_args(dtype=dt, m=m, n=n, k=k, a=ops.a.data_ptr(), b=ops.b.data_ptr(),
-                          d=ops.d.data_ptr(), sfa=None if ops.sfa is None else ops.sfa.data_ptr(),
-                          sfb=None if ops.sfb is None else ops.sfb.data_ptr(),
-                          status=status.data_ptr(), clock_out=clock_buf.data_ptr(), **knobs)
-    rc, info = pkg.query(gargs)
-    if rc != pkg.OK:
-        raise SystemExit(f"cannot implement: {info.reason.decode()}")
+    gargs.status = status.data_ptr()
     L = pkg.lib()
     launch = L.gemm_sm100a_launch
     argp = C.byref(gargs)
@@ -339,6 +400,7 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize(dev)
     barrier()
     ms = start.elapsed_time(end)
+    from microbench_blackwell_b200 import nsplit
     ms_max = nsplit.max_over_ranks(ms, device=dev)
     rc, detail = pkg.read_status(status.data_ptr(), st)
     if rc != 0:
@@ -349,37 +411,26 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     achieved = flop / (ms / args.steps * 1e-3) / 1e12          # this rank's kernel, per launch
     clocks = sampler.summary()
     clocks["kernel_sm_mhz"] = kernel_mhz(clock_buf)
-
-    # ---------------------------------------------------------- optional all-gather of D (N > 1)
-    allgather = None
-    if world > 1:
-        with torch.cuda.stream(stream):
-            nsplit.gather_columns(ops.d, n * world)                 # warm-up
-            stream.synchronize()
-            barrier()
-            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            g0.record(stream)
-            full = nsplit.gather_columns(ops.d, n * world)
-            g1.record(stream)
-        g1.synchronize()
-        ag_ms = nsplit.max_over_ranks(g0.elapsed_time(g1), device=dev)
-        recv = (world - 1) * ops.d.numel() * ops.d.element_size()
-        allgather = {"ms": ag_ms, "bytes_received_per_rank": recv,
-                     "GBps_per_rank": recv / (ag_ms * 1e-3) / 1e9, "collective": "ncclAllGather (torch.distributed)"}
-        del full
+    gargs.status = None
 
     # ---------------------------------------------------------- the reference's kernel family, same box
     ref_full = run_reference_cutlass_full(pkg, ops, gargs, stream, wl["dtype"], args.steps) if world == 1 else None
 
     # ---------------------------------------------------------- end to end (host buffers)
     e2e = run_e2e(pkg, ops, gargs, dev, stream, args, world, local_rank)
+    del ops
+    torch.cuda.empty_cache()
 
-    # ---------------------------------------------------------- the other dtypes
+    # ---------------------------------------------------------- the other BASELINE configurations
     per_dtype = None
     if not args.no_per_dtype:
-        del ops
-        torch.cuda.empty_cache()
-        per_dtype = run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, clocks.get("sm_mhz"))
+        per_dtype = run_per_dtype(pkg, args, dev, stream, world, rank, local_rank)
+
+    extras = {}
+    if world == 1 and not args.no_per_dtype:
+        extras["config2_stage_sweep"] = run_stage_sweep(pkg, args, dev, stream)
+        extras["tma_hbm_probe"] = run_tma_probe(pkg, dev, stream)
+        extras["config1_bf16_256"] = run_config1(pkg, args, dev, stream, extras["tma_hbm_probe"])
 
     # ---------------------------------------------------------- single-CTA mainloop (reference experiment)
     single = run_single_cta(pkg, wl, dev, stream) if (rank == 0 and wl["dtype"] in SINGLE_CTA_CFG) else None
@@ -387,7 +438,6 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     if rank != 0:
         return
     peaks = measured_peaks()
-    sm_mhz = clocks.get("sm_mhz")
     umma_peak = measured_umma_peak(pkg, wl["dtype"], dev)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -398,7 +448,8 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     line = {
         "metric": "GEMM TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if wl.get("split") == "strong" else "weak",
+        "vs_baseline": None,
         "dtype": wl["dtype"], "data": "synthetic (seeded, generated on device)",
         "config": config_block(wl, world, args),
         "roofline": {"bound": "tensor", "achieved": achieved,
@@ -408,33 +459,28 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
                      "peak_source": peak_src,
                      "traffic": ncu_traffic(args.workload),
                      "algorithmic_bytes": m * k * elem_bytes(wl["dtype"]) + n * k * elem_bytes(wl["dtype"]) + m * n * 2},
-        "sol_umma": {"pct_measured_umma_peak": 100.0 * achieved / umma_peak["tflops"],
-                     "umma_peak_tflops": umma_peak["tflops"], "umma_flop_per_clk_per_sm": umma_peak["flop_per_clk_per_sm"],
-                     "umma_sm_mhz": umma_peak["sm_mhz"], "source": umma_peak["source"],
-                     "reference_flop_per_clk_per_sm": REF_UMMA_FLOP_PER_CLK_SM[wl["dtype"]],
-                     "pct_at_gemm_clock": pct_at_clock(achieved, umma_peak, clocks["kernel_sm_mhz"]),
-                     "gemm_sm_mhz": clocks["kernel_sm_mhz"],
-                     "pct_at_max_clock": 100.0 * achieved / (umma_peak["flop_per_clk_per_sm"] * 148 * SM_MAX_MHZ * 1e6 / 1e12)},
+        "sol_umma": sol_block(achieved, umma_peak, clocks["kernel_sm_mhz"], wl["dtype"]),
         "clocks": clocks,
         "e2e": e2e,
         "gpu_launches": args.steps,
         "cpu_baseline": cpu,
         "single_cta": single,
         "reference_cutlass_full": ref_full,
-        "allgather": allgather,
         "per_dtype": per_dtype,
+        **extras,
         "kernel": {"grid": info.grid_ctas, "stages": info.stages, "tile": [info.tile_m, info.tile_n, info.tile_k],
-                   "smem_bytes": info.smem_bytes, "tmem_columns": info.tmem_columns},
+                   "smem_bytes": info.smem_bytes, "tmem_columns": info.tmem_columns,
+                   "epilogue_staging_buffers": info.epilogue_staging_buffers},
     }
     print(json.dumps(line), flush=True)
 
 
 PER_DTYPE = [
-    # (label, workload, scaling): weak = every rank does the full per-GPU problem on its own
-    # N slab; strong = the workload's N is split across the ranks (config 5).
-    ("e4m3_config3", "e4m3_16384_2sm", "weak"),
-    ("nvfp4_config4", "nvfp4_mlp", "weak"),
-    ("e4m3_nsplit_config5", "e4m3_nsplit", "strong"),
+    # (label, workload): configs 3-5 and fp8 at 8192^3 (north_star's >= 90 % target)
+    ("e4m3_config3", "e4m3_16384_2sm"),
+    ("e4m3_8192", "e4m3_8192"),
+    ("nvfp4_config4", "nvfp4_mlp"),
+    ("e4m3_nsplit_config5", "e4m3_nsplit"),
 ]
 
 
@@ -452,6 +498,21 @@ def pct_at_clock(tflops, umma_peak, mhz):
     return 100.0 * tflops / (umma_peak["flop_per_clk_per_sm"] * 148 * mhz * 1e6 / 1e12)
 
 
+def sol_block(tflops_per_gpu, umma_peak, gemm_mhz, dtype):
+    """SOL against the own tcgen05 probe.  Primary: the per-clock efficiency (TFLOP/s over
+    the probe's FLOP/clk/SM x 148 SMs at the GEMM's own measured clock), which cannot exceed
+    100 %.  The ratio to the whole-GPU probe at the probe's clock is secondary: the probe,
+    a pure tensor load, is power-capped to a different clock than a GEMM."""
+    return {"pct_umma_peak_at_gemm_clock": pct_at_clock(tflops_per_gpu, umma_peak, gemm_mhz),
+            "gemm_sm_mhz": gemm_mhz,
+            "umma_flop_per_clk_per_sm": umma_peak["flop_per_clk_per_sm"],
+            "reference_flop_per_clk_per_sm": REF_UMMA_FLOP_PER_CLK_SM[dtype],
+            "pct_umma_peak_at_max_clock": 100.0 * tflops_per_gpu / (umma_peak["flop_per_clk_per_sm"] * 148 * SM_MAX_MHZ * 1e6 / 1e12),
+            "secondary_pct_of_whole_gpu_probe": 100.0 * tflops_per_gpu / umma_peak["tflops"],
+            "whole_gpu_probe_tflops": umma_peak["tflops"], "whole_gpu_probe_sm_mhz": umma_peak["sm_mhz"],
+            "probe": umma_peak["source"]}
+
+
 def measured_umma_peak(pkg, dtype_name: str, dev) -> dict:
     """Whole-GPU tcgen05 dense peak of this GPU for one dtype (CTA pairs on every SM,
     non-zero operands), from the library's probe -- the SOL denominator."""
@@ -463,32 +524,20 @@ def measured_umma_peak(pkg, dtype_name: str, dev) -> dict:
     return r
 
 
-def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
+def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank):
     """Time the other BASELINE configurations (fewer steps) for the per-dtype metric."""
     import torch
     import torch.distributed as dist
     from microbench_blackwell_b200 import nsplit
     out = {}
     steps = max(5, min(args.steps, 20))
-    for label, name, scaling in PER_DTYPE:
+    L = pkg.lib()
+    sp = C.c_void_p(stream.cuda_stream)
+    for label, name in PER_DTYPE:
         wl = WORKLOADS[name]
-        m, k = wl["m"], wl["k"]
-        if scaling == "strong":
-            slab = nsplit.partition(wl["n"], world, rank, align=wl["knobs"]["tile_n"])
-        else:
-            slab = nsplit.partition(wl["n"] * world, world, rank, align=wl["knobs"]["tile_n"])
-        n = slab.n_local
-        dt = dtype_code(pkg, wl["dtype"])
-        ops = pkg.make_operands(dt, m, n, k, seed=args.seed, a_dist=dist_code(pkg, wl["a"][0]), a_scale=wl["a"][1],
-                                b_dist=dist_code(pkg, wl["b"][0]), b_scale=wl["b"][1], n0=slab.n0,
-                                device=dev, stream=stream.cuda_stream)
-        clock_buf = torch.zeros(2, dtype=torch.int64, device=dev)
-        g = pkg.make_args(dtype=dt, m=m, n=n, k=k, a=ops.a.data_ptr(), b=ops.b.data_ptr(), d=ops.d.data_ptr(),
-                          sfa=None if ops.sfa is None else ops.sfa.data_ptr(),
-                          sfb=None if ops.sfb is None else ops.sfb.data_ptr(), clock_out=clock_buf.data_ptr(),
-                          **wl["knobs"])
-        L = pkg.lib()
-        sp = C.c_void_p(stream.cuda_stream)
+        knobs = dict(wl["knobs"])
+        slab = slab_for(wl, knobs, world, rank)
+        ops, g, clock_buf, _ = make_gemm(pkg, wl, knobs, slab, dev, stream, args.seed)
         # Untimed settle (>= 3 launches, ~0.25 s): the clock reaches this configuration's
         # own power-capped steady state instead of the previous configuration's.
         settle_end = time.perf_counter() + 0.25
@@ -508,24 +557,160 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank, sm_mhz):
         s1.synchronize()
         ms = nsplit.max_over_ranks(s0.elapsed_time(s1) / steps, device=dev)
         gemm_mhz = kernel_mhz(clock_buf)
-        flop_total = pkg.flops(m, n, k) * world
+        flop_total = pkg.flops(ops.m, ops.n, ops.k) * world
         tf = flop_total / (ms * 1e-3) / 1e12
         per_gpu = tf / world
-        ref_full = run_reference_cutlass_full(pkg, ops, g, stream, wl["dtype"], steps) if world == 1 else None
+        rec = {"workload": name, "baseline_config": wl["config"],
+               "scaling": "strong" if wl.get("split") == "strong" else "weak",
+               "m": ops.m, "n_total": slab.n_total, "n_per_gpu": ops.n, "k": ops.k, "knobs": knobs, "steps": steps,
+               "ms_per_step": ms, "tflops": tf, "tflops_per_gpu": per_gpu}
+        g.clock_out = None
+        rec["reference_cutlass_full"] = run_reference_cutlass_full(pkg, ops, g, stream, wl["dtype"], steps) if world == 1 else None
+        if wl.get("split") == "strong" and world > 1:
+            rec["gather"] = run_nsplit_gather(pkg, ops, g, slab, dev, stream, world, rank, local_rank, ms)
         peak = measured_umma_peak(pkg, wl["dtype"], dev)
-        out[label] = {"workload": name, "baseline_config": wl["config"], "scaling": scaling,
-                      "m": m, "n_total": n * world, "k": k, "knobs": wl["knobs"], "steps": steps,
-                      "ms_per_step": ms, "tflops": tf, "tflops_per_gpu": per_gpu,
-                      "umma_peak_tflops": peak["tflops"], "umma_peak_sm_mhz": peak["sm_mhz"],
-                      "pct_measured_umma_peak": 100.0 * per_gpu / peak["tflops"],
-                      # The probe's clock under power capping can fall below the GEMM's, which
-                      # lifts the ratio above 100 %; this one uses the SM's maximum clock instead.
-                      "pct_umma_peak_at_max_clock": 100.0 * per_gpu / (peak["flop_per_clk_per_sm"] * 148 * SM_MAX_MHZ * 1e6 / 1e12),
-                      "gemm_sm_mhz": gemm_mhz,
-                      "pct_umma_peak_at_gemm_clock": pct_at_clock(per_gpu, peak, gemm_mhz),
-                      "reference_cutlass_full": ref_full}
+        rec["sol_umma"] = sol_block(per_gpu, peak, gemm_mhz, wl["dtype"])
+        rec["pct_umma_peak_at_gemm_clock"] = rec["sol_umma"]["pct_umma_peak_at_gemm_clock"]
+        out[label] = rec
         del ops
         torch.cuda.empty_cache()
+    return out
+
+
+def run_nsplit_gather(pkg, ops, g, slab, dev, stream, world, rank, local_rank, gemm_ms):
+    """Config 5's optional output gather, timed three ways at N GPUs (max over ranks):
+    the GEMM alone (gemm_ms), ncclAllGather of this configuration's own bf16 D slices,
+    and the fused GEMM + gather (gemm_sm100a_launch_gather: the epilogue also stores each
+    staged block into every other GPU's full D, reached by CUDA IPC over NVLink).  The
+    fused result is checked bit for bit against the NCCL-gathered D."""
+    import torch
+    import torch.distributed as dist
+    from microbench_blackwell_b200 import nsplit
+    out = {"gemm_ms": gemm_ms}
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        full = nsplit.gather_columns(ops.d, slab.n_total)                 # warm-up
+        stream.synchronize()
+        times = []
+        for _ in range(3):
+            dist.barrier(device_ids=[local_rank])
+            ev0.record(stream)
+            full = nsplit.gather_columns(ops.d, slab.n_total)
+            ev1.record(stream)
+            ev1.synchronize()
+            times.append(ev0.elapsed_time(ev1))
+    ag_ms = nsplit.max_over_ranks(min(times), device=dev)
+    recv = (world - 1) * ops.d.numel() * ops.d.element_size()
+    out["nccl_allgather"] = {"ms": ag_ms, "bytes_received_per_rank": recv,
+                             "GBps_per_rank": recv / (ag_ms * 1e-3) / 1e9,
+                             "gemm_plus_allgather_ms": gemm_ms + ag_ms}
+    try:
+        out["fused"] = nsplit.fused_gather_timing(pkg, g, ops, slab, full, stream, dev, local_rank)
+    except Exception as e:       # a box without peer access between the ranks' GPUs
+        out["fused"] = {"unavailable": repr(e)[:200]}
+        dist.barrier(device_ids=[local_rank])
+    del full
+    return out
+
+
+def run_stage_sweep(pkg, args, dev, stream):
+    """BASELINE config 2 exactly as stated: the 1-SM 128x256x64 tile at 8192^3 with stages
+    swept 2..8 (interleaved bursts, medians).  Stages that do not fit in shared memory are
+    reported as the can't-implement rows of the reference's sweep (results.csv:462-465)."""
+    import torch
+    from microbench_blackwell_b200 import nsplit
+    wl = WORKLOADS["bf16_8192_1sm"]
+    slab = nsplit.partition(wl["n"], 1, 0)
+    ops, g0, _, _ = make_gemm(pkg, wl, dict(wl["knobs"]), slab, dev, stream, args.seed)
+    L = pkg.lib()
+    sp = C.c_void_p(stream.cuda_stream)
+    rows, fns, keep = [], {}, []
+    for s in range(2, 9):
+        g = pkg.make_args(dtype=ops.dtype, m=ops.m, n=ops.n, k=ops.k, a=ops.a.data_ptr(), b=ops.b.data_ptr(),
+                          d=ops.d.data_ptr(), **dict(wl["knobs"], stages=s))
+        rc, info = pkg.query(g)
+        if rc != pkg.OK:
+            rows.append({"stages": s, "cannot_implement": info.reason.decode()})
+            continue
+        keep.append(g)
+        fns[f"S{s}"] = (lambda g=g: L.gemm_sm100a_launch(C.byref(g), sp))
+        rows.append({"stages": s})
+    res = interleaved(stream, fns, pkg.flops(ops.m, ops.n, ops.k), rounds=4)
+    for r in rows:
+        key = f"S{r['stages']}"
+        if res and key in res:
+            r["tflops"] = res[key]["tflops"]
+    del ops
+    torch.cuda.empty_cache()
+    return {"tile": [128, 256, 64], "cta_group": 1, "rows": rows}
+
+
+def run_tma_probe(pkg, dev, stream):
+    """The TMA-2D HBM read roof (the reference's tma2d_throughput sweep points, 2 GiB read
+    once after an L2 flush): the memory-side denominator for config 1 and skinny shapes."""
+    import torch
+    buf = torch.empty(2 << 30, dtype=torch.uint8, device=dev)
+    flush = torch.empty(pkg.L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    pts = []
+    with torch.cuda.stream(stream):
+        for rows, stages in ((256, 1), (128, 1), (64, 2), (32, 4), (16, 4)):
+            best = max((pkg.tma_read_probe(buf, box_rows=rows, stages=stages, flush=flush, device=dev)
+                        for _ in range(2)), key=lambda r: r["GBps"])
+            pts.append({"box": [128, rows], "stages": stages, "bytes_in_flight_per_sm": best["bytes_in_flight_per_sm"],
+                        "GBps": best["GBps"], "cycles_per_tma": best["cycles_per_tma"]})
+    del buf, flush
+    torch.cuda.empty_cache()
+    top = max(pts, key=lambda r: r["GBps"])
+    return {"points": pts, "roof_GBps": top["GBps"],
+            "reference_roof_GBps": 7260.0, "reference_source": "tma2d_throughput/tma2d_tput_results.csv:25 (ncu DRAM counter)",
+            "method": "bytes / CUDA-event time of one probe launch over 2 GiB after an L2 flush"}
+
+
+def run_config1(pkg, args, dev, stream, probe):
+    """BASELINE config 1 (bf16 256^3), latency-bound: per-launch device time from a
+    stream of back-to-back launches and from a CUDA graph of them, against the time the
+    384 KiB of A, B and D take at the measured TMA read roof."""
+    import torch
+    from microbench_blackwell_b200 import nsplit
+    wl = WORKLOADS["bf16_256"]
+    ops, g, _, _ = make_gemm(pkg, wl, dict(wl["knobs"]), nsplit.partition(256, 1, 0), dev, stream, args.seed)
+    L = pkg.lib()
+    sp = C.c_void_p(stream.cuda_stream)
+    n = 2000
+    for _ in range(20):
+        L.gemm_sm100a_launch(C.byref(g), sp)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        L.gemm_sm100a_launch(C.byref(g), sp)
+    e1.record(stream)
+    e1.synchronize()
+    us_stream = e0.elapsed_time(e1) / n * 1e3
+    out = {"us_per_launch_stream": us_stream}
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(100):
+                L.gemm_sm100a_launch(C.byref(g), C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        graph.replay()
+        stream.synchronize()
+        e0.record(stream)
+        for _ in range(n // 100):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+        out["us_per_launch_graph"] = e0.elapsed_time(e1) / n * 1e3
+        del graph
+    except Exception as e:
+        out["graph"] = {"unavailable": repr(e)[:200]}
+    us = min(v for k, v in out.items() if k.startswith("us_per"))
+    bytes_moved = 3 * 256 * 256 * 2
+    out.update({"tflops": pkg.flops(256, 256, 256) / (us * 1e-6) / 1e12,
+                "bytes_moved": bytes_moved, "GBps": bytes_moved / (us * 1e-6) / 1e9,
+                "memory_roof_us": bytes_moved / (probe["roof_GBps"] * 1e9) * 1e6,
+                "note": "2 output tiles on 2 SMs: bound by launch and pipeline latency, not by HBM or tensor throughput"})
+    del ops
+    torch.cuda.empty_cache()
     return out
 
 
@@ -654,8 +839,9 @@ CUTLASS_REF_KERNELS = {
 def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
     """The reference's own CUTLASS kernel family (oracle/_ref/libcutlass_ref.so, the
     cutlass_gemm_bench.cu:101-156 type chain, plus its 2SM and Nvf4 schedules) on the same
-    operands over the whole GPU, each kernel timed interleaved with ours (2 rounds each)
-    so both see the same clock state.  Informational: the reference itself runs one CTA."""
+    operands over the whole GPU, interleaved with ours in alternating bursts (6 rounds,
+    medians) so every kernel sees the same power-capped clock state.  Informational:
+    the reference itself runs one CTA."""
     import torch
     kernels = CUTLASS_REF_KERNELS.get(dtype)
     lib = ROOT / "oracle" / "_ref" / "libcutlass_ref.so"
@@ -672,24 +858,8 @@ def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
     d_ref = torch.empty_like(ops.d)
     sfa = None if ops.sfa is None else ops.sfa.data_ptr()
     sfb = None if ops.sfb is None else ops.sfb.data_ptr()
-
-    def ours():
-        return L.gemm_sm100a_launch(C.byref(gargs), sp)
-
-    def timed(fn, n):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(n):
-            if fn() != 0:
-                return None
-        e1.record(stream)
-        e1.synchronize()
-        return e0.elapsed_time(e1) / n
-
-    flop = pkg.flops(ops.m, ops.n, ops.k)
-    n = max(5, min(steps, 50))
-    out = {"steps_per_round": n, "rounds": 2, "kernels": {}}
-    best = None
+    fns = {"ours": lambda: L.gemm_sm100a_launch(C.byref(gargs), sp)}
+    out = {"kernels": {}}
     for kid, desc in kernels.items():
         def cut(kid=kid):
             return R.cutlass_ref_run(kid, ops.a.data_ptr(), ops.b.data_ptr(), sfa, sfb, d_ref.data_ptr(),
@@ -698,26 +868,25 @@ def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
         if rc != 0:
             out["kernels"][desc] = {"unavailable": f"cutlass_ref_run returned {rc}"}
             continue
-        for _ in range(2):
-            cut(); ours()
-        stream.synchronize()
-        t_cut, t_ours = [], []
-        for _ in range(2):
-            t_ours.append(timed(ours, n))
-            t_cut.append(timed(cut, n))
-        if None in t_cut or None in t_ours:
-            out["kernels"][desc] = {"unavailable": "launch failed"}
+        fns[desc] = cut
+    stream.synchronize()
+    res = interleaved(stream, fns, pkg.flops(ops.m, ops.n, ops.k))
+    if res is None:
+        return {"unavailable": "launch failed"}
+    out["rounds"] = res["_rounds"]
+    out["launches_per_burst"] = res["_launches_per_burst"]
+    out["tflops_ours_interleaved"] = res["ours"]["tflops"]
+    best = None
+    for desc in fns:
+        if desc == "ours":
             continue
-        rec = {"tflops_cutlass": flop / (min(t_cut) * 1e-3) / 1e12,
-               "tflops_ours_interleaved": flop / (min(t_ours) * 1e-3) / 1e12}
-        rec["ours_over_cutlass"] = rec["tflops_ours_interleaved"] / rec["tflops_cutlass"]
+        rec = {"tflops_cutlass": res[desc]["tflops"], "ours_over_cutlass": 1.0 / res[desc]["ratio_to_ours"]}
         out["kernels"][desc] = rec
         if best is None or rec["tflops_cutlass"] > best[1]["tflops_cutlass"]:
             best = (desc, rec)
     if best is not None:
         out["best_cutlass_kernel"] = best[0]
         out["tflops_cutlass"] = best[1]["tflops_cutlass"]
-        out["tflops_ours_interleaved"] = best[1]["tflops_ours_interleaved"]
         out["ours_over_best_cutlass"] = best[1]["ours_over_cutlass"]
     return out
 

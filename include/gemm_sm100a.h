@@ -21,9 +21,10 @@
  * with one unsigned e4m3 scale per 16 consecutive K elements of each row.
  *
  * Ownership: the caller owns every buffer (A, B, scale factors, D and the
- * optional status word). The launcher allocates nothing, throws nothing and
- * keeps no mutable global state apart from a once-initialised driver entry
- * point, so concurrent calls on different streams or devices are safe.
+ * optional status word). The launcher allocates nothing and throws nothing;
+ * its only global state is a once-initialised driver entry point and a
+ * mutex-guarded record of the kernels whose shared-memory limit it has raised
+ * on each device, so concurrent calls on different streams or devices are safe.
  */
 #ifndef GEMM_SM100A_H
 #define GEMM_SM100A_H

@@ -20,8 +20,9 @@
 //               TMEM lane quadrant each), alpha scale, bf16 round, column-major
 //               stores.
 // Warps 0 and 1 run their loops converged, so addresses and descriptors are
-// warp-uniform, with every TMA / mbarrier / tcgen05 issue predicated on one
-// elected lane; the loops are instantiated per stage shape (atoms x MMA K
+// warp-uniform; the producer's TMA / mbarrier issue is predicated on one
+// elected lane, and the MMA warp issues each stage's tcgen05 ops from that lane
+// inside a branch; the loops are instantiated per stage shape (atoms x MMA K
 // steps).  The accumulator is double-buffered in TMEM (2 x BN columns) when it
 // fits, so the epilogue of tile i overlaps the mainloop of tile i+1; a single
 // accumulator is drained into registers and released before D is written.
@@ -56,10 +57,10 @@ using namespace sm100;
 #define GEMM_TRACE 0            // 1: log CTA 0's pipeline events (trace builds only)
 #endif
 #ifndef GEMM_WIDE_EPI_WARPS
-#define GEMM_WIDE_EPI_WARPS 8   // epilogue warps of a 512-column tile (8 or 16)
+#define GEMM_WIDE_EPI_WARPS 16  // epilogue warps of a 512-column tile (8 or 16)
 #endif
 #ifndef GEMM_WIDE_EARLY_RELEASE
-#define GEMM_WIDE_EARLY_RELEASE 1  // 1: a TMEM-filling accumulator is drained into registers and released
+#define GEMM_WIDE_EARLY_RELEASE 0  // 1: a 512-column accumulator is drained into registers and released
                                    //    before D is written; 0: written chunk by chunk, released after the last read
 #endif
 
@@ -86,7 +87,8 @@ struct IntC { static constexpr int value = V; };
 
 // Threads per CTA: producer warp + MMA warp + EPI_WARPS epilogue warps.
 // Epilogue warps: 4 (one per TMEM lane quadrant), or GEMM_WIDE_EPI_WARPS for a
-// 512-column tile, whose single accumulator is drained into registers.
+// 512-column tile (one accumulator filling TMEM): 16 warps read it in four
+// column groups, which shortens the time the MMA warp waits for it.
 __host__ __device__ constexpr int epi_warps_for(int bn) { return bn > 256 ? GEMM_WIDE_EPI_WARPS : 4; }
 __host__ __device__ constexpr int threads_for(int bn) { return 64 + 32 * epi_warps_for(bn); }
 constexpr int kSmemLimit = 232448;      // 227 KiB of opt-in dynamic shared memory per CTA
@@ -95,6 +97,10 @@ constexpr int kMaxStages = 32;
 constexpr int kMaxGatherPeers = 7;   // peer D destinations of the fused gather (8 GPUs per box)
 constexpr int kDefaultL2Prefetch = 0;         // k-blocks of L2 prefetch ahead of the ring (0 = off)
 constexpr int kMinSmemPerCta = 120 * 1024;  // > half of the SM's 228 KiB: at most one CTA per SM
+#ifndef GEMM_ACC_OVERLAP
+#define GEMM_ACC_OVERLAP 64     // overlapped accumulator positions for 256-wide NVFP4 tiles (columns; 0 = off)
+#endif
+constexpr int kAccOverlap = GEMM_ACC_OVERLAP;
 
 enum Role : uint32_t { ROLE_PRODUCER = 1, ROLE_MMA = 2, ROLE_EPILOGUE = 3, ROLE_DRAIN = 4 };
 
@@ -129,6 +135,8 @@ struct KernelParams {
   int32_t l2_prefetch;    // k-blocks the L2 prefetch cursor runs ahead of the loads (0 = off)
   unsigned long long* clock_out;   // optional: CTA 0's [cycles, ns] over the launch
   int32_t num_acc;        // accumulator buffers in TMEM (2 = epilogue overlaps the next tile)
+  int32_t acc_overlap;    // > 0: one accumulator barrier, two positions (0 and BN - acc_overlap)
+                          // alternating per tile; the epilogue frees the shared columns first
   float beta;             // D = alpha * acc + beta * C (C read only when beta != 0)
   const __nv_bfloat16* c; // C, same layout as D, leading dimension ldc
   int64_t ldc;
@@ -466,9 +474,9 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     });
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Converged warp: descriptors and addresses are warp-uniform; every
-    // tcgen05 op is predicated on one lane, elected once, so its commits
-    // track all of its MMAs.
+    // Converged warp: descriptors and addresses are warp-uniform; each
+    // stage's tcgen05 ops are issued by one lane, elected once, so its
+    // commits track all of its MMAs.
     if (leader) with_stage_shape([&](auto na_c, auto ks_c) {
       constexpr int NA = decltype(na_c)::value;
       constexpr int KS = decltype(ks_c)::value;
@@ -480,6 +488,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      int pos = 0;            // accumulator position of the next tile when positions overlap
       bool ok = true;
       bool issued = false;
       // Loop-invariant parameters in registers.
@@ -500,7 +509,8 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (!__all_sync(0xffffffffu, wt)) { ok = false; break; }
         TRACE_EVENT(2u, 3u, acc);
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(p.acc_overlap ? pos * (BN - p.acc_overlap) : acc * BN);
+        if (p.acc_overlap) pos ^= 1;
         bool ready = false;   // next stage's data already seen (probed after the previous commit)
         for (int kb = 0; kb < n_kb; ++kb) {
           const bool w = ready || wait_bar<CG == 2>(full_bar + 8u * stage, phase, ctl, ROLE_MMA, stage);
@@ -509,13 +519,18 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           tc_fence_after();
           const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
           const uint32_t bbase = sbase + (uint32_t)NA * a_bytes;
+          // The stage's tcgen05 ops are issued by one thread inside a branch (the
+          // operands above are warp-uniform): in pair mode a predicated issue by the
+          // whole warp made every tcgen05.cp and tcgen05.mma cost ~70 cycles.
+          if (issue) {
           if constexpr (DT == 2) {
             // Copy this stage's scale factors into TMEM (columns after the
             // accumulators), then issue the block-scaled MMAs.
             const uint32_t sf_base = bbase + (uint32_t)NA * b_bytes;
             constexpr int NSF = NA * 4;
             constexpr uint32_t SF_STAGE_COLS = (uint32_t)NSF * (SF_COLS_A + SF_COLS_B);
-            const uint32_t sfa_t = tmem_base + (uint32_t)(n_acc * BN) + (uint32_t)sf_slot * SF_STAGE_COLS;
+            const uint32_t sf0 = p.acc_overlap ? (uint32_t)(2 * BN - p.acc_overlap) : (uint32_t)(n_acc * BN);
+            const uint32_t sfa_t = tmem_base + sf0 + (uint32_t)sf_slot * SF_STAGE_COLS;
             const uint32_t sfb_t = sfa_t + (uint32_t)NSF * SF_COLS_A;
             if (++sf_slot == n_sf_slots) sf_slot = 0;
 #pragma unroll
@@ -554,6 +569,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           }
           if constexpr (CG == 2) mma_commit_pair(empty_bar + 8u * stage, 0x3, issue);
           else mma_commit(empty_bar + 8u * stage, issue);
+          }
           TRACE_EVENT(2u, 2u, stage);
           issued = true;
           if (++stage == n_stages) { stage = 0; phase ^= 1u; }
@@ -602,6 +618,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint32_t chunk_no = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
+    int pos = 0;                                    // accumulator position (overlapped positions)
     const uint32_t leader_tempty = CG == 2 ? mapa_shared(tempty_bar, 0) : tempty_bar;
     unsigned trace_i = 0;
     (void)trace_i;
@@ -621,7 +638,10 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const int64_t row = m0 + r_loc;
       const int64_t n0 = (int64_t)un * BN;
       const bool row_ok = (int)lane < q_rows && row < p.m;
-      const uint32_t t_row = tmem_base + ((32u * q) << 16) + (uint32_t)(acc * BN);
+      const int ov = p.acc_overlap;
+      const int cur_pos = pos;                         // accumulator position of this tile
+      if (ov) pos ^= 1;
+      const uint32_t t_row = tmem_base + ((32u * q) << 16) + (uint32_t)(ov ? cur_pos * (BN - ov) : acc * BN);
 
       auto release_acc = [&]() {
         tc_fence_before();
@@ -754,7 +774,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       };
 
       if constexpr (COLS % 32 == 0) {
-        if (GEMM_WIDE_EARLY_RELEASE && p.num_acc == 1 && beta == 0.f) {
+        if ((BN <= 256 || GEMM_WIDE_EARLY_RELEASE) && p.num_acc == 1 && !ov && beta == 0.f) {
           // Single accumulator (the tile fills TMEM): drain it into registers
           // as packed bf16 pairs, release it at once so the next tile's MMAs
           // start, then write D while that mainloop runs.
@@ -781,12 +801,21 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
       }
       // Chunk by chunk: the accumulator is released right after its last
-      // chunk has been read from TMEM, before that chunk is written out.
+      // chunk has been read from TMEM, before that chunk is written out.  With
+      // overlapped positions the columns the other position shares are read
+      // first (the tail of position 0, the head of position 1) and the
+      // accumulator is released as soon as they are in registers.
+      constexpr int NCH = COLS / CW;
+      const int ov_ch = ov / CW;
+      const int first = (ov && cur_pos == 0) ? NCH - ov_ch : 0;
+      const int release_after = ov ? ov_ch - 1 : NCH - 1;
 #pragma unroll 1
-      for (int cc = 0; cc < COLS; cc += CW) {
+      for (int i = 0; i < NCH; ++i) {
+        const int ci = first + i < NCH ? first + i : first + i - NCH;
+        const int cc = ci * CW;
         uint32_t r[CW], o[CW / 2];
         tmem_chunk(t_row + (uint32_t)(c_begin + cc), r);
-        if (cc + CW == COLS) release_acc();
+        if (i == release_after) release_acc();
         if (beta != 0.f) convert_c(c_begin + cc, r, o); else convert(r, o);
         emit(c_begin + cc, o);
       }
@@ -833,6 +862,7 @@ struct Resolved {
   uint32_t a_atom_bytes, b_atom_bytes, sf_stage_bytes, stage_bytes;
   int64_t smem_bytes;
   int tmem_cols, num_acc, threads, sf_slots;
+  int acc_overlap;                  // columns the two accumulator positions share (0 = disjoint)
   uint32_t row_bytes;
   int cw, stg_bufs;                 // epilogue chunk width; staging buffers per group (0 = direct stores)
   uint32_t stg_bytes, stg_offset;
@@ -969,14 +999,23 @@ int resolve(const GemmArgs* a, Resolved& r) {
   // next tile's mainloop), else one.  NVFP4 scale factors then take as many
   // per-stage slots (up to 4, at most the stage count) as the columns left allow.
   r.num_acc = 2 * r.bn + sf_cols <= 512 ? 2 : 1;
+  r.acc_overlap = 0;
+  if (r.num_acc == 1 && sf_cols > 0 && r.bn == 256 && kAccOverlap > 0 && 2 * r.bn - kAccOverlap + sf_cols <= 512) {
+    // NVFP4 256-wide tile: the second accumulator position starts kAccOverlap
+    // columns before the first one ends, which leaves the top columns for the
+    // scale factors.  The epilogue reads the shared columns first and then
+    // releases the accumulator, so the next tile's MMAs overlap the rest of it.
+    r.acc_overlap = kAccOverlap;
+  }
+  const int acc_cols = r.acc_overlap ? 2 * r.bn - r.acc_overlap : r.num_acc * r.bn;
   r.sf_slots = 1;
   if (sf_cols > 0) {
-    r.sf_slots = (512 - r.num_acc * r.bn) / sf_cols;
+    r.sf_slots = (512 - acc_cols) / sf_cols;
     if (r.sf_slots > 4) r.sf_slots = 4;
     if (r.sf_slots > r.stages) r.sf_slots = r.stages;
     if (r.sf_slots < 1) r.sf_slots = 1;
   }
-  const int cols = r.num_acc * r.bn + r.sf_slots * sf_cols;
+  const int cols = acc_cols + r.sf_slots * sf_cols;
   if (cols > 512) FAIL("TMEM: %d columns needed (accumulator + scales) > 512", cols);
   r.tmem_cols = next_pow2_cols(cols);
   r.threads = threads_for(r.bn);
@@ -1060,6 +1099,26 @@ KernelFn pick_bn(int bn) {
     }
   }
   return nullptr;
+}
+
+// Each kernel's dynamic shared-memory limit is raised to the 227 KiB maximum
+// once per device (launches then pass their own size), so a launch makes no
+// attribute call; that keeps launches cheap and capturable in CUDA graphs.
+std::mutex g_attr_mu;
+struct AttrSet { KernelFn fn; int dev; };
+AttrSet g_attr_set[1024];
+int g_attr_n = 0;
+
+bool ensure_smem_attr(KernelFn fn, int dev) {
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  for (int i = 0; i < g_attr_n; ++i)
+    if (g_attr_set[i].fn == fn && g_attr_set[i].dev == dev) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (g_attr_n < 1024) g_attr_set[g_attr_n++] = {fn, dev};
+  return true;
 }
 
 KernelFn pick_kernel(int dt, int cg, int bn) {
@@ -1157,6 +1216,7 @@ static int launch_impl(const GemmArgs* args, void* const* peers, int n_peers, vo
   p.sf_stage_bytes = r.sf_stage_bytes;
   p.idesc = make_idesc(r.dt, r.bm, r.bn > 256 ? 256 : r.bn);
   p.num_acc = r.num_acc;
+  p.acc_overlap = r.acc_overlap;
   p.alpha = r.alpha_eff;
   p.beta = a.beta;
   p.c = reinterpret_cast<const __nv_bfloat16*>(a.c);
@@ -1181,10 +1241,7 @@ static int launch_impl(const GemmArgs* args, void* const* peers, int n_peers, vo
 
   KernelFn fn = pick_kernel(r.dt, r.cg, r.bn);
   if (!fn) return GEMM_ERR_CANNOT_IMPLEMENT;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r.smem_bytes) != cudaSuccess) {
-    cudaGetLastError();
-    return GEMM_ERR_LAUNCH;
-  }
+  if (!ensure_smem_attr(fn, guard.dev)) return GEMM_ERR_LAUNCH;
 
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
@@ -1218,8 +1275,9 @@ PFN_memGetAddressRange g_addr_range = nullptr;
 std::once_flag g_addr_range_once;
 
 // True when [ptr, ptr + bytes) lies inside one device allocation.  The range
-// is queried with the owning device current (its primary context), then the
-// caller's device is restored.
+// is queried in the caller's context (which also holds mappings opened from
+// other processes by CUDA IPC), else with the owning device current (its
+// primary context), after which the caller's device is restored.
 bool block_inside_allocation(const void* ptr, size_t bytes, int owner, int current) {
   std::call_once(g_addr_range_once, [] {
     void* fn = nullptr;
@@ -1229,11 +1287,14 @@ bool block_inside_allocation(const void* ptr, size_t bytes, int owner, int curre
       g_addr_range = reinterpret_cast<PFN_memGetAddressRange>(fn);
   });
   if (!g_addr_range) return false;
-  if (owner != current && cudaSetDevice(owner) != cudaSuccess) { cudaGetLastError(); return false; }
   CUdeviceptr base = 0;
   size_t size = 0;
-  const CUresult r = g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
-  if (owner != current) cudaSetDevice(current);
+  CUresult r = g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS && owner != current) {
+    if (cudaSetDevice(owner) != cudaSuccess) { cudaGetLastError(); return false; }
+    r = g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+    cudaSetDevice(current);
+  }
   if (r != CUDA_SUCCESS) return false;
   const uintptr_t p = reinterpret_cast<uintptr_t>(ptr);
   return p >= base && bytes <= size && p - base <= size - bytes;

@@ -58,3 +58,76 @@ def gather_columns(d_local, n_total: int):
     full = torch.empty((n_total, m), dtype=d_local.dtype, device=d_local.device)
     dist.all_gather_into_tensor(full, d_local.contiguous())
     return full
+
+
+def fused_gather_timing(pkg, g, ops, slab, full_ref, stream, dev, local_rank, reps: int = 3) -> dict:
+    """Time the fused GEMM + all-gather (gemm_sm100a_launch_gather) of this rank's slab.
+
+    Every rank allocates its full column-major D (cudaMalloc, exact size) and shares it
+    with the others by CUDA IPC; each launch then writes this rank's D block into its own
+    full D and, over NVLink, into the same block of every peer's full D.  Returns the
+    max-over-ranks time of the fastest of `reps` launches and whether the gathered D
+    equals `full_ref` (the NCCL all-gather result) bit for bit.  Every rank takes the same
+    collective steps, and the IPC mappings are closed and the buffer freed before return."""
+    import ctypes as C
+    import torch
+    import torch.distributed as dist
+    from cuda.bindings import runtime as rt
+
+    def ok(err):
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"CUDA runtime error {err}")
+
+    world, rank = dist.get_world_size(), dist.get_rank()
+    m = ops.m
+    nbytes = slab.n_total * m * 2
+    err, base = rt.cudaMalloc(nbytes)
+    ok(err)
+    opened = []
+    try:
+        err, handle = rt.cudaIpcGetMemHandle(base)
+        ok(err)
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle.reserved))
+        peers = {}
+        for j in range(world):
+            if j == rank:
+                continue
+            h = rt.cudaIpcMemHandle_t()
+            h.reserved = handles[j]
+            err, ptr = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+            ok(err)
+            opened.append(ptr)
+            peers[j] = int(ptr)
+        off = slab.n0 * m * 2                                   # this rank's column block
+        args = pkg.GemmArgs.from_buffer_copy(g)
+        args.d, args.ldd = int(base) + off, m
+        peer_ptrs = [peers[j] + off for j in sorted(peers)]
+        st = stream.cuda_stream
+        pkg.launch_gather(args, peer_ptrs, st)                 # warm-up
+        stream.synchronize()
+        times = []
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(reps):
+            dist.barrier(device_ids=[local_rank])
+            e0.record(stream)
+            pkg.launch_gather(args, peer_ptrs, st)
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        dist.barrier(device_ids=[local_rank])                  # every peer's stores have landed
+        got = torch.empty_like(full_ref)
+        ok(rt.cudaMemcpy(got.data_ptr(), base, nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice)[0])
+        same = bool(torch.equal(got, full_ref))
+        ms = max_over_ranks(min(times), device=dev)
+        sent = (world - 1) * slab.n_local * m * 2
+        return {"ms": ms, "bytes_sent_per_rank": sent, "GBps_per_rank": sent / (ms * 1e-3) / 1e9,
+                "matches_nccl_allgather": same,
+                "path": "gemm_sm100a_launch_gather: staged epilogue blocks stored into every peer's full D "
+                        "(CUDA IPC mappings, NVLink), no loads from peers"}
+    finally:
+        dist.barrier(device_ids=[local_rank])
+        for ptr in opened:
+            rt.cudaIpcCloseMemHandle(ptr)
+        dist.barrier(device_ids=[local_rank])
+        rt.cudaFree(base)

@@ -170,7 +170,7 @@ def test_epilogue_staging_buffers(pkg):
     """The TMA-store epilogue stages D in shared memory when it fits next to the
     ring (the stage count, and so can_implement, never depends on it)."""
     cases = [(dict(tile_n=256, tile_k=64, stages=4), 2),                       # bf16 128x256x64 S4
-             (dict(tile_n=512, tile_k=64, cta_group=2), 2),                    # pair 256x512, two groups
+             (dict(tile_n=512, tile_k=64, cta_group=2), 1),                    # pair 256x512, four groups
              (dict(tile_n=128, tile_k=64), 0),                                 # 7 stages fill shared memory
              (dict(tile_n=256, tile_k=64, stages=4, flags=pkg.FLAG_DIRECT_EPILOGUE), 0)]
     for knobs, bufs in cases:

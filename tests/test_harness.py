@@ -10,11 +10,37 @@ HARNESS = ROOT / "microbench-blackwell_b200" / "harness"
 HEADER = "M,N,K,TILE_M,TILE_N,TILE_K,STAGES,dtype,time_ms,TFLOPS"   # cutlass_gemm_mainloop/sweep.sh:21
 
 
-def test_sweep_writes_the_reference_header_and_failure_rows():
-    text = (HARNESS / "sweep.sh").read_text()
-    assert f'echo "{HEADER}" > "$OUTFILE"' in text
-    assert '"# FAILED: $cfg"' in text and '"# BUILD_FAILED: $cfg"' in text
-    assert "STAGE_LIST=(0 2 3 4 5 6 7 8)" in text             # sweep.sh:23
+def _sweep():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("sweep_for_tests", HARNESS / "sweep.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_sweep_writes_the_reference_header_stages_and_failure_rows():
+    sw = _sweep()
+    assert sw.HEADER == HEADER
+    assert sw.STAGE_LIST == (0, 2, 3, 4, 5, 6, 7, 8)                    # sweep.sh:23
+    assert sw.K_EXPERIMENT == 131072 and (sw.WARMUP, sw.TIMED) == (1, 20)  # cutlass_gemm_bench.cu:52-55
+    text = (HARNESS / "sweep.py").read_text()
+    assert '"# FAILED: {cfg_text(p)}"' in text and '"# BUILD_FAILED: {cfg_text(p)}"' in text
+    line = sw.csv_line(128, 256, 64, 4, 0, 1.0)
+    assert line.split(",")[:8] == ["128", "256", "131072", "128", "256", "64", "4", "BF16"]
+    assert abs(float(line.split(",")[9]) - 2 * 128 * 256 * 131072 / 1e-3 / 1e12) < 1e-3
+
+
+def test_full_sweep_covers_every_reference_point():
+    """The reference's lists (sweep.sh:28-65) at every stage count, in the full scope."""
+    sw = _sweep()
+    pts = set(sw.sweep_points("full"))
+    tile_n = (16, 32, 64, 128, 192, 256)
+    for dt, ks in ((0, (16, 32, 64, 128, 256)), (1, (32, 64, 128, 256, 512))):
+        for tm in (64, 128):
+            for tn in tile_n:
+                for tk in ks:
+                    for s in (0, 2, 3, 4, 5, 6, 7, 8):
+                        assert (tm, tn, tk, s, dt) in pts
 
 
 def test_harness_builds_with_reference_knobs(tmp_path):
