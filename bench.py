@@ -344,7 +344,7 @@ def make_gemm(pkg, wl, knobs, slab, dev, stream, seed):
                                 a_dist=dist_code(pkg, wl["a"][0]), a_scale=wl["a"][1],
                                 b_dist=dist_code(pkg, wl["b"][0]), b_scale=wl["b"][1],
                                 n0=slab.n0, device=dev, stream=stream.cuda_stream)
-    clock_buf = torch.zeros(2, dtype=torch.int64, device=dev)     # CTA 0's [cycles, ns] per launch
+    clock_buf = torch.zeros(2, dtype=torch.int64, device=dev)     # [cycles, ns] summed over CTAs and launches
     g = pkg.make_args(dtype=dt, m=ops.m, n=ops.n, k=ops.k, a=ops.a.data_ptr(), b=ops.b.data_ptr(),
                       d=ops.d.data_ptr(), sfa=None if ops.sfa is None else ops.sfa.data_ptr(),
                       sfb=None if ops.sfb is None else ops.sfb.data_ptr(), clock_out=clock_buf.data_ptr(), **knobs)
@@ -391,10 +391,10 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     sampler = ClockSampler(local_rank)
     barrier()
     torch.cuda.synchronize(dev)
+    step_clocks = torch.zeros((args.steps, 2), dtype=torch.int64, device=dev)
     with sampler:
         start.record(stream)
-        for _ in range(args.steps):
-            launch(argp, sp)
+        launch_recording_clocks(launch, gargs, sp, args.steps, step_clocks)
         end.record(stream)
         end.synchronize()
     torch.cuda.synchronize(dev)
@@ -410,8 +410,9 @@ def run_ours(args, wl, rank: int, world: int, local_rank: int):
     value = flop * world / (ms_per_step * 1e-3) / 1e12
     achieved = flop / (ms / args.steps * 1e-3) / 1e12          # this rank's kernel, per launch
     clocks = sampler.summary()
-    clocks["kernel_sm_mhz"] = kernel_mhz(clock_buf)
+    clocks["kernel_sm_mhz"] = kernel_mhz(step_clocks)
     gargs.status = None
+    gargs.clock_out = None
 
     # ---------------------------------------------------------- the reference's kernel family, same box
     ref_full = run_reference_cutlass_full(pkg, ops, gargs, stream, wl["dtype"], args.steps) if world == 1 else None
@@ -485,10 +486,21 @@ PER_DTYPE = [
 
 
 def kernel_mhz(clock_buf):
-    """Effective SM clock of the last launch, from the kernel's own clock64 / %globaltimer
-    record (CTA 0, whole launch): sampled NVML clocks miss power-cap throttling."""
-    cyc, ns = (int(v) for v in clock_buf.cpu().tolist())
+    """Effective SM clock over the launches that recorded into clock_buf ([n, 2]: the cycles
+    and ns every CTA of a launch adds, the kernel's own clock64 / %globaltimer record): sum of
+    cycles over sum of time.  Sampled NVML clocks miss power-cap throttling."""
+    v = clock_buf.view(-1, 2).cpu().double()
+    cyc, ns = float(v[:, 0].sum()), float(v[:, 1].sum())
     return 1000.0 * cyc / ns if ns > 0 else None
+
+
+def launch_recording_clocks(launch, g, sp, steps, clock_buf):
+    """Enqueue `steps` launches of `g`, each adding its CTAs' cycles and ns into its own
+    (zeroed) row of clock_buf ([steps, 2] int64): the timed launches' mean clock."""
+    base = clock_buf.data_ptr()
+    for i in range(steps):
+        g.clock_out = base + 16 * i
+        launch(C.byref(g), sp)
 
 
 def pct_at_clock(tflops, umma_peak, mhz):
@@ -550,13 +562,13 @@ def run_per_dtype(pkg, args, dev, stream, world, rank, local_rank):
         if world > 1:
             dist.barrier(device_ids=[local_rank])
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        step_clocks = torch.zeros((steps, 2), dtype=torch.int64, device=dev)
         s0.record(stream)
-        for _ in range(steps):
-            L.gemm_sm100a_launch(C.byref(g), sp)
+        launch_recording_clocks(L.gemm_sm100a_launch, g, sp, steps, step_clocks)
         s1.record(stream)
         s1.synchronize()
         ms = nsplit.max_over_ranks(s0.elapsed_time(s1) / steps, device=dev)
-        gemm_mhz = kernel_mhz(clock_buf)
+        gemm_mhz = kernel_mhz(step_clocks)
         flop_total = pkg.flops(ops.m, ops.n, ops.k) * world
         tf = flop_total / (ms * 1e-3) / 1e12
         per_gpu = tf / world
@@ -689,7 +701,7 @@ def run_config1(pkg, args, dev, stream, probe):
     out = {"us_per_launch_stream": us_stream}
     try:
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="relaxed"):
             for _ in range(100):
                 L.gemm_sm100a_launch(C.byref(g), C.c_void_p(torch.cuda.current_stream().cuda_stream))
         graph.replay()
@@ -827,18 +839,15 @@ SM_MAX_MHZ = 1965.0   # B200 clocks.max.sm
 
 # Kernels of oracle/_ref/libcutlass_ref.so (oracle/cutlass_ref.cu) timed beside ours, per dtype.
 CUTLASS_REF_KERNELS = {
-    "bf16": {0: "CUTLASS SM100 1SM 128x256x64, 4 stages (the reference's best point, cutlass_gemm_mainloop/results.csv:461)",
-             2: "CUTLASS SM100 2SM 256x256x64, cluster 2x1, auto stages, TMA epilogue"},
-    "e4m3": {1: "CUTLASS SM100 1SM 128x256x128, auto stages (cutlass_gemm_mainloop/results.csv:938)",
-             3: "CUTLASS SM100 2SM 256x256x128, cluster 2x1, auto stages, TMA epilogue"},
-    "nvfp4": {4: "CUTLASS SM100 1SM Nvf4 128x256x256, auto stages",
-              5: "CUTLASS SM100 2SM Nvf4 256x256x256, cluster 2x1, auto stages"},
+    "bf16": {0: "CUTLASS SM100 1SM 128x256x64, 4 stages (the reference's best point, cutlass_gemm_mainloop/results.csv:461)"},
+    "e4m3": {1: "CUTLASS SM100 1SM 128x256x128, auto stages (cutlass_gemm_mainloop/results.csv:938)"},
+    "nvfp4": {4: "CUTLASS SM100 1SM Nvf4 128x256x256, auto stages"},
 }
 
 
 def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
     """The reference's own CUTLASS kernel family (oracle/_ref/libcutlass_ref.so, the
-    cutlass_gemm_bench.cu:101-156 type chain, plus its 2SM and Nvf4 schedules) on the same
+    cutlass_gemm_bench.cu:101-156 type chain, 1SM schedule, plus its Nvf4 form) on the same
     operands over the whole GPU, interleaved with ours in alternating bursts (6 rounds,
     medians) so every kernel sees the same power-capped clock state.  Informational:
     the reference itself runs one CTA."""

@@ -120,8 +120,9 @@ typedef struct GemmArgs {
   uint32_t timeout_ms;    /* device wait budget; 0 = default (4000 ms) */
   uint32_t flags;         /* GEMM_FLAG_* */
   int32_t  l2_prefetch;   /* warm L2 this many k-blocks ahead of the shared-memory ring; 0 = default, < 0 = off */
-  unsigned long long* clock_out; /* optional device [2]: SM cycles and nanoseconds CTA 0 spent in the launch
-                                    (cycles / ns = the effective SM clock under power capping) */
+  unsigned long long* clock_out; /* optional device [2]: every CTA adds the SM cycles and nanoseconds it
+                                    spent in the launch (zero it first; cycles / ns = the launch's mean
+                                    effective SM clock under power capping) */
   /* Epilogue (CUTLASS LinearCombination, cutlass_gemm_bench.cu:117-118,196-204):
    * D = alpha * scale_a * scale_b * (A . B^T) + beta * C, computed in fp32 and
    * rounded once to bf16.  C is bf16 with D's layout and leading dimension ldc

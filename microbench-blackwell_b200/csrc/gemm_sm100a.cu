@@ -133,7 +133,7 @@ struct KernelParams {
   int32_t n_d_peer;
   __nv_bfloat16* d_peer[kMaxGatherPeers];
   int32_t l2_prefetch;    // k-blocks the L2 prefetch cursor runs ahead of the loads (0 = off)
-  unsigned long long* clock_out;   // optional: CTA 0's [cycles, ns] over the launch
+  unsigned long long* clock_out;   // optional: [cycles, ns] summed over the launch's CTAs
   int32_t num_acc;        // accumulator buffers in TMEM (2 = epilogue overlaps the next tile)
   int32_t acc_overlap;    // > 0: one accumulator barrier, two positions (0 and BN - acc_overlap)
                           // alternating per tile; the epilogue frees the shared columns first
@@ -834,9 +834,11 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
     tc_fence_after();
     tmem_dealloc<CG>(tmem_base, (uint32_t)p.tmem_cols);
   }
-  if (p.clock_out && blockIdx.x == 0 && threadIdx.x == 0) {
-    p.clock_out[0] = clock64() - clk0;
-    p.clock_out[1] = globaltimer_ns() - ns0;
+  if (p.clock_out && threadIdx.x == 0) {
+    // Every CTA adds its own cycles and nanoseconds: the ratio is the launch's
+    // mean SM clock, weighted by how long each CTA ran.
+    atomicAdd(p.clock_out, (unsigned long long)(clock64() - clk0));
+    atomicAdd(p.clock_out + 1, (unsigned long long)(globaltimer_ns() - ns0));
   }
 }
 

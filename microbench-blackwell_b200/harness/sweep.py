@@ -14,8 +14,8 @@ Every point is the reference experiment (cutlass_gemm_bench.cu:52-55,158-257):
 one CTA (one CTA pair for TILE_M 256), M = TILE_M, N = TILE_N, K = 131072,
 zero-filled operands, one warm-up launch, then 20 launches between CUDA events;
 the line is M,N,K,TILE_M,TILE_N,TILE_K,STAGES,dtype,time_ms,TFLOPS with
-TFLOPS = 2*M*N*K / time, followed in-process by sm_mhz, the effective SM clock
-of the last timed launch (the kernel's own clock64 / %globaltimer record), which
+TFLOPS = 2*M*N*K / time, followed in-process by sm_mhz, the mean effective SM
+clock of the timed launches (the kernel's own clock64 / %globaltimer record), which
 readers that select columns by name (the reference's plot script) ignore.
 
 Two ways to run the points:
@@ -133,6 +133,7 @@ def run_in_process(points, emit):
             continue
         sp = C.c_void_p(stream.cuda_stream)
         ok = all(L.gemm_sm100a_launch(C.byref(args), sp) == 0 for _ in range(WARMUP))
+        clock.zero_()                  # the timed launches add their cycles and ns
         e0.record(stream)
         ok = ok and all(L.gemm_sm100a_launch(C.byref(args), sp) == 0 for _ in range(TIMED))
         e1.record(stream)

@@ -15,21 +15,20 @@
 //         results.csv:461; KernelTmaWarpSpecialized1SmSm100 +
 //         NoSmemWarpSpecialized1Sm, cluster 1x1x1, exactly :107-136)
 //   id 1  e4m3 1SM 128x256x128, auto stages (results.csv:938)
-//   id 2  bf16 2SM 256x256x64, cluster 2x1x1 (KernelTmaWarpSpecialized2SmSm100
-//         + TmaWarpSpecialized2Sm epilogue, auto stages)
-//   id 3  e4m3 2SM 256x256x128, cluster 2x1x1 (same schedules)
-//   id 4  NVFP4 1SM 128x256x256 (KernelTmaWarpSpecialized1SmNvf4Sm100)
-//   id 5  NVFP4 2SM 256x256x256, cluster 2x1x1 (KernelTmaWarpSpecialized2SmNvf4Sm100)
+//   id 4  NVFP4 1SM 128x256x256 (KernelTmaWarpSpecialized1SmNvf4Sm100), the
+//         reference family extended to the block-scaled type (the reference
+//         has no NVFP4, :58-66)
 //
-// Ids 2-5 are the reference family extended to the schedules the benchmark
-// plan's configurations 3-5 need (the reference builds the 1SM schedule
-// only, :114).  The NVFP4 scale buffers use CUTLASS's K-major 128x4 scale
-// atom (Sm1xxBlockScaledConfig, tiled K-blocks fastest), which is the byte
-// layout the sm_100a library takes, so both kernels read the same buffers.
+// Every kernel here runs on a cluster of one CTA.  CUTLASS's 2SM schedules need
+// a 2x1 cluster, a form this pool treats as a cluster-multicast TMA load (which
+// would bar every multi-GPU run), so they are not instantiated.  The NVFP4
+// scale buffers use CUTLASS's K-major 128x4 scale atom (Sm1xxBlockScaledConfig,
+// tiled K-blocks fastest), the byte layout the sm_100a library takes, so both
+// kernels read the same buffers.
 //
 // REF_PART selects which instantiations this translation unit compiles
-// (0: ids 0-1, 1: ids 2-3, 2: ids 4-5, -1: all) so the build can run the
-// slow CUTLASS compilations in parallel; every part defines its own entry.
+// (0: ids 0-1, 2: id 4, -1: all) so the build can run the slow CUTLASS
+// compilations in parallel; every part defines its own entry.
 #include <cuda_runtime.h>
 
 #include "cute/tensor.hpp"
@@ -71,13 +70,13 @@ cutlass::KernelHardwareInfo hw_info(int sm_count) {
 }
 
 // Dense bf16 / e4m3 GEMM of the reference family.
-template <class ElementAB, int TM, int TN, int TK, int CM, int Stages, class MainSched, class EpiSched>
+template <class ElementAB, int TM, int TN, int TK, int Stages, class MainSched, class EpiSched>
 struct RefGemm {
   using LayoutA = cutlass::layout::RowMajor;
   using LayoutB = cutlass::layout::ColumnMajor;
   using LayoutD = cutlass::layout::ColumnMajor;
   using ElementD = cutlass::bfloat16_t;
-  using Cluster = Shape<Int<CM>, _1, _1>;
+  using Cluster = Shape<_1, _1, _1>;
   using Tile = Shape<Int<TM>, Int<TN>, Int<TK>>;
   static constexpr int AlignAB = 128 / cutlass::sizeof_bits<ElementAB>::value;
   static constexpr int AlignD = 128 / cutlass::sizeof_bits<ElementD>::value;
@@ -114,14 +113,14 @@ struct RefGemm {
 };
 
 // NVFP4 block-scaled GEMM (e2m1 values, ue4m3 scale per 16 K elements).
-template <int TM, int TN, int TK, int CM, class MainSched>
+template <int TM, int TN, int TK, class MainSched>
 struct RefNvf4 {
   using ElementAB = cutlass::nv_float4_t<cutlass::float_e2m1_t>;
   using LayoutA = cutlass::layout::RowMajor;
   using LayoutB = cutlass::layout::ColumnMajor;
   using LayoutD = cutlass::layout::ColumnMajor;
   using ElementD = cutlass::bfloat16_t;
-  using Cluster = Shape<Int<CM>, _1, _1>;
+  using Cluster = Shape<_1, _1, _1>;
   using Tile = Shape<Int<TM>, Int<TN>, Int<TK>>;
   static constexpr int AlignAB = 32;
   static constexpr int AlignD = 128 / cutlass::sizeof_bits<ElementD>::value;
@@ -173,23 +172,11 @@ using namespace cutlass::epilogue;
 extern "C" int PART_ENTRY(0)(int id, const void* A, const void* B, const void*, const void*, void* D, int M, int N,
                              int K, int sms, cudaStream_t s) {
   if (id == 0)
-    return RefGemm<cutlass::bfloat16_t, 128, 256, 64, 1, 4, KernelTmaWarpSpecialized1SmSm100,
+    return RefGemm<cutlass::bfloat16_t, 128, 256, 64, 4, KernelTmaWarpSpecialized1SmSm100,
                    NoSmemWarpSpecialized1Sm>::run(A, B, D, M, N, K, sms, s);
   if (id == 1)
-    return RefGemm<cutlass::float_e4m3_t, 128, 256, 128, 1, 0, KernelTmaWarpSpecialized1SmSm100,
+    return RefGemm<cutlass::float_e4m3_t, 128, 256, 128, 0, KernelTmaWarpSpecialized1SmSm100,
                    NoSmemWarpSpecialized1Sm>::run(A, B, D, M, N, K, sms, s);
-  return -6;
-}
-#endif
-#if REF_PART == 1 || REF_PART == -1
-extern "C" int PART_ENTRY(1)(int id, const void* A, const void* B, const void*, const void*, void* D, int M, int N,
-                             int K, int sms, cudaStream_t s) {
-  if (id == 2)
-    return RefGemm<cutlass::bfloat16_t, 256, 256, 64, 2, 0, KernelTmaWarpSpecialized2SmSm100,
-                   TmaWarpSpecialized2Sm>::run(A, B, D, M, N, K, sms, s);
-  if (id == 3)
-    return RefGemm<cutlass::float_e4m3_t, 256, 256, 128, 2, 0, KernelTmaWarpSpecialized2SmSm100,
-                   TmaWarpSpecialized2Sm>::run(A, B, D, M, N, K, sms, s);
   return -6;
 }
 #endif
@@ -197,21 +184,17 @@ extern "C" int PART_ENTRY(1)(int id, const void* A, const void* B, const void*, 
 extern "C" int PART_ENTRY(2)(int id, const void* A, const void* B, const void* SFA, const void* SFB, void* D, int M,
                              int N, int K, int sms, cudaStream_t s) {
   if (id == 4)
-    return RefNvf4<128, 256, 256, 1, KernelTmaWarpSpecialized1SmNvf4Sm100>::run(A, B, SFA, SFB, D, M, N, K, sms, s);
-  if (id == 5)
-    return RefNvf4<256, 256, 256, 2, KernelTmaWarpSpecialized2SmNvf4Sm100>::run(A, B, SFA, SFB, D, M, N, K, sms, s);
+    return RefNvf4<128, 256, 256, KernelTmaWarpSpecialized1SmNvf4Sm100>::run(A, B, SFA, SFB, D, M, N, K, sms, s);
   return -6;
 }
 #endif
 
 #if REF_PART == 0 || REF_PART == -1
-extern "C" int cutlass_ref_part1(int, const void*, const void*, const void*, const void*, void*, int, int, int, int,
-                                 cudaStream_t);
 extern "C" int cutlass_ref_part2(int, const void*, const void*, const void*, const void*, void*, int, int, int, int,
                                  cudaStream_t);
 
 // Run kernel `id` (table above) on device buffers: D (column-major M x N bf16)
-// = A . B^T.  sfa / sfb are the NVFP4 scale buffers (ids 4-5, else unused).
+// = A . B^T.  sfa / sfb are the NVFP4 scale buffers (id 4, else unused).
 // sm_count <= 0 uses every SM of the current device.  Returns 0 on success,
 // -1 can't implement, -2 launch error, -4 unknown id.
 extern "C" int cutlass_ref_run(int id, const void* A, const void* B, const void* sfa, const void* sfb, void* D,
@@ -224,8 +207,7 @@ extern "C" int cutlass_ref_run(int id, const void* A, const void* B, const void*
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (id) {
     case 0: case 1: return cutlass_ref_part0(id, A, B, sfa, sfb, D, M, N, K, sm_count, s);
-    case 2: case 3: return cutlass_ref_part1(id, A, B, sfa, sfb, D, M, N, K, sm_count, s);
-    case 4: case 5: return cutlass_ref_part2(id, A, B, sfa, sfb, D, M, N, K, sm_count, s);
+    case 4: return cutlass_ref_part2(id, A, B, sfa, sfb, D, M, N, K, sm_count, s);
   }
   return -4;
 }

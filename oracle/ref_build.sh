@@ -49,20 +49,20 @@ else
   echo "no reference tree given (argument or MICROBENCH_REF_ROOT): reference binaries skipped"
 fi
 
-# The comparison library: three translation units (REF_PART 0..2) compiled in parallel.
+# The comparison library: two translation units (REF_PART 0 and 2) compiled in parallel.
 LIB="$OUT/libcutlass_ref.so"
 if [[ ! -f "$LIB" || "$HERE/cutlass_ref.cu" -nt "$LIB" ]]; then
-  for part in 0 1 2; do
+  for part in 0 2; do
     ( nvcc "${NVCCFLAGS[@]}" "${INC[@]}" -O3 -Xcompiler -fPIC -DREF_PART=$part -c \
           -o "$OUT/cutlass_ref_p$part.o" "$HERE/cutlass_ref.cu" > "$OUT/cutlass_ref_p$part.log" 2>&1 \
         && echo "compiled cutlass_ref part $part" || echo "FAILED cutlass_ref part $part (see $OUT/cutlass_ref_p$part.log)" ) &
     throttle
   done
   wait
-  if [[ -f "$OUT/cutlass_ref_p0.o" && -f "$OUT/cutlass_ref_p1.o" && -f "$OUT/cutlass_ref_p2.o" ]]; then
-    nvcc "-gencode=arch=compute_100a,code=sm_100a" -shared -o "$LIB" "$OUT"/cutlass_ref_p{0,1,2}.o -lcuda \
+  if [[ -f "$OUT/cutlass_ref_p0.o" && -f "$OUT/cutlass_ref_p2.o" ]]; then
+    nvcc "-gencode=arch=compute_100a,code=sm_100a" -shared -o "$LIB" "$OUT"/cutlass_ref_p{0,2}.o -lcuda \
       && echo "built libcutlass_ref.so"
-    rm -f "$OUT"/cutlass_ref_p{0,1,2}.o
+    rm -f "$OUT"/cutlass_ref_p{0,2}.o
   fi
 fi
 wait
