@@ -704,12 +704,13 @@ def run_config1(pkg, args, dev, stream, probe):
         with torch.cuda.graph(graph, stream=stream, capture_error_mode="relaxed"):
             for _ in range(100):
                 L.gemm_sm100a_launch(C.byref(g), C.c_void_p(torch.cuda.current_stream().cuda_stream))
-        graph.replay()
-        stream.synchronize()
-        e0.record(stream)
-        for _ in range(n // 100):
+        with torch.cuda.stream(stream):              # replay() launches on the current stream
             graph.replay()
-        e1.record(stream)
+            stream.synchronize()
+            e0.record(stream)
+            for _ in range(n // 100):
+                graph.replay()
+            e1.record(stream)
         e1.synchronize()
         out["us_per_launch_graph"] = e0.elapsed_time(e1) / n * 1e3
         del graph

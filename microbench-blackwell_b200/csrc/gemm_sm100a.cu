@@ -20,10 +20,9 @@
 //               TMEM lane quadrant each), alpha scale, bf16 round, column-major
 //               stores.
 // Warps 0 and 1 run their loops converged, so addresses and descriptors are
-// warp-uniform; the producer's TMA / mbarrier issue is predicated on one
-// elected lane, and the MMA warp issues each stage's tcgen05 ops from that lane
-// inside a branch; the loops are instantiated per stage shape (atoms x MMA K
-// steps).  The accumulator is double-buffered in TMEM (2 x BN columns) when it
+// warp-uniform; TMA, mbarrier and tcgen05 issue is predicated on one elected
+// lane (in CTA-pair kernels that lane issues inside a branch instead); the
+// loops are instantiated per stage shape (atoms x MMA K steps).  The accumulator is double-buffered in TMEM (2 x BN columns) when it
 // fits, so the epilogue of tile i overlaps the mainloop of tile i+1; a single
 // accumulator is drained into registers and released before D is written.
 //
@@ -191,17 +190,16 @@ __device__ __noinline__ void raise_abort(const SharedCtl& c, uint32_t role, uint
 }
 
 // Bounded wait for phase `parity` of mbarrier `bar`; false when aborted.
-// Each probe lets the hardware suspend the thread until the phase completes
-// (or kWaitHintNs passes), so a completed phase is noticed at once; the
-// abort flag is checked after every probe and the timer every 8 probes.
-constexpr uint32_t kWaitHintNs = 200000;
+// The probes are plain try_wait (no suspend-time hint: resuming a suspended
+// thread added latency to every pipeline round trip); the abort flag is
+// checked after every probe and the timer every 8 probes.
 template <bool kCluster>
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const SharedCtl& c,
                                          uint32_t role, uint32_t idx) {
   if (kCluster ? mbar_test_wait_cluster(bar, parity) : mbar_test_wait(bar, parity)) return true;
   uint64_t t0 = 0;
   for (uint32_t probe = 1;; ++probe) {
-    if (kCluster ? mbar_try_wait_cluster_hint(bar, parity, kWaitHintNs) : mbar_try_wait_hint(bar, parity, kWaitHintNs))
+    if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity))
       return true;
     if (ld_shared_volatile_u32(c.abort_addr)) return false;
     if ((probe & 7u) == 1u) {
@@ -409,6 +407,10 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
           const uint32_t fb = full_bar + 8u * stage;
           const uint32_t target = CG == 2 ? leader_full + 8u * stage : fb;
+          // In pair mode one thread issues the stage's expect_tx and loads inside
+          // a branch (cheaper there than a whole-warp predicated issue); 1-SM
+          // kernels issue from the converged warp, predicated on the elected lane.
+          if (CG == 1 || issue) {
           mbar_arrive_expect_tx(fb, tx_bytes, leader ? issue : 0u);
 #pragma unroll
           for (int ka = 0; ka < NA; ++ka) {
@@ -450,6 +452,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 bulk_load(sf_base + (uint32_t)NSF * 512u * (1 + bb), sfb_src, (uint32_t)NSF * 512u, target, policy, issue);
               }
             }
+          }
           }
           TRACE_EVENT(1u, 2u, stage);
           issued_mask |= 1u << stage;
@@ -519,10 +522,12 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           tc_fence_after();
           const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
           const uint32_t bbase = sbase + (uint32_t)NA * a_bytes;
-          // The stage's tcgen05 ops are issued by one thread inside a branch (the
-          // operands above are warp-uniform): in pair mode a predicated issue by the
-          // whole warp made every tcgen05.cp and tcgen05.mma cost ~70 cycles.
-          if (issue) {
+          // Pair mode: the stage's tcgen05 ops are issued by one thread inside a
+          // branch -- a predicated issue by the whole warp made every two-CTA
+          // tcgen05.cp and tcgen05.mma cost ~70 cycles.  1-SM kernels keep the
+          // converged, predicated issue, whose operands stay warp-uniform (small
+          // tiles issue a stage every few dozen cycles).
+          if (CG == 1 || issue) {
           if constexpr (DT == 2) {
             // Copy this stage's scale factors into TMEM (columns after the
             // accumulators), then issue the block-scaled MMAs.
