@@ -400,8 +400,13 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const int32_t m0 = um * MMA_M + (int32_t)cta_rank * BM;
         const int32_t n0 = un * BN + (int32_t)cta_rank * B_BOX;
         for (int kb = 0; kb < n_kb; ++kb) {
-          const bool w = wait_bar<false>(empty_bar + 8u * stage, phase ^ 1u, ctl, ROLE_PRODUCER, stage);
-          if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+          // Fast path: the slot is already free, take it with no warp vote (a
+          // per-stage vote made this loop the bottleneck of small single-CTA
+          // tiles).  Only a real wait votes, over the lanes that took it.
+          if (!mbar_test_wait(empty_bar + 8u * stage, phase ^ 1u)) {
+            const bool w = wait_bar<false>(empty_bar + 8u * stage, phase ^ 1u, ctl, ROLE_PRODUCER, stage);
+            if (!__all_sync(__activemask(), w)) { ok = false; break; }
+          }
           TRACE_EVENT(1u, 1u, stage);
           if (p.l2_prefetch > 0) pf_step();
           const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
@@ -459,6 +464,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == n_stages) { stage = 0; phase ^= 1u; }
         }
+        ok = __all_sync(0xffffffffu, ok);   // one uniform abort decision per tile
       }
       if (!ok && (CG == 1 || leader)) {
         // Let every load already issued land before the CTA may exit.  In a
@@ -516,8 +522,13 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (p.acc_overlap) pos ^= 1;
         bool ready = false;   // next stage's data already seen (probed after the previous commit)
         for (int kb = 0; kb < n_kb; ++kb) {
+          // No warp vote per stage (it cost the MMA-bound small tiles 4-9 %):
+          // every lane probes the same barrier in the same instruction, and the
+          // tcgen05 ops below are single-thread, so a lane that left early
+          // blocks nothing.  The vote after the k-block loop makes the abort
+          // decision uniform before the next warp-collective step.
           const bool w = ready || wait_bar<CG == 2>(full_bar + 8u * stage, phase, ctl, ROLE_MMA, stage);
-          if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+          if (!w) { ok = false; break; }
           TRACE_EVENT(2u, 1u, stage);
           tc_fence_after();
           const uint32_t sbase = ring + (uint32_t)stage * st_bytes;
@@ -583,6 +594,7 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
           ready = CG == 2 ? mbar_test_wait_cluster(full_bar + 8u * stage, phase)
                           : mbar_test_wait(full_bar + 8u * stage, phase);
         }
+        ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         if constexpr (CG == 2) mma_commit_pair(tfull_bar + 8u * acc, 0x3, issue);
         else mma_commit(tfull_bar + 8u * acc, issue);

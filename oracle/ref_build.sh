@@ -28,7 +28,8 @@ jobs=0
 throttle() { jobs=$((jobs + 1)); if (( jobs >= MAX_JOBS )); then wait -n || true; jobs=$((jobs - 1)); fi; }
 
 # The reference's single-CTA configurations (TILE_M,TILE_N,TILE_K,STAGES,DTYPE_ID):
-# the best BF16 / FP8 points of results.csv (:461, :938) and their stage sweeps.
+# the best BF16 / FP8 points of results.csv (:461, :938) and their stage sweeps,
+# and small TILE_M = 64 tiles, whose time is the per-stage loop cost.
 SRC="$REF/cutlass_gemm_mainloop/cutlass_gemm_bench.cu"
 if [[ -n "$REF" && -f "$SRC" ]]; then
   CONFIGS=(
@@ -36,6 +37,8 @@ if [[ -n "$REF" && -f "$SRC" ]]; then
     "128,192,64,0,0" "128,128,64,0,0"
     "128,256,128,0,1" "128,256,128,2,1" "128,256,128,3,1" "128,256,128,4,1"
     "128,192,128,0,1" "128,128,128,0,1"
+    "64,16,16,0,0" "64,16,64,0,0" "64,64,64,0,0" "64,16,16,4,0" "64,128,64,0,0"
+    "64,16,32,0,1" "64,64,128,0,1"
   )
   for cfg in "${CONFIGS[@]}"; do
     IFS=',' read -r TM TN TK S D <<< "$cfg"
