@@ -850,7 +850,8 @@ def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
     """The reference's own CUTLASS kernel family (oracle/_ref/libcutlass_ref.so, the
     cutlass_gemm_bench.cu:101-156 type chain, 1SM schedule, plus its Nvf4 form) on the same
     operands over the whole GPU, interleaved with ours in alternating bursts (6 rounds,
-    medians) so every kernel sees the same power-capped clock state.  Informational:
+    medians) so every kernel sees the same power-capped clock state.  For bf16 the vendor
+    GEMM (cuBLAS through torch.mm) joins the same bursts (`vendor_cublas`).  Informational:
     the reference itself runs one CTA."""
     import torch
     kernels = CUTLASS_REF_KERNELS.get(dtype)
@@ -879,10 +880,24 @@ def run_reference_cutlass_full(pkg, ops, gargs, stream, dtype, steps):
             out["kernels"][desc] = {"unavailable": f"cutlass_ref_run returned {rc}"}
             continue
         fns[desc] = cut
+    cublas = "cuBLAS (torch.mm, bf16)"
+    if dtype == "bf16":
+        # The vendor GEMM on the same operands, as a comparison only: D^T = B . A^T
+        # in D's own layout (ops.d is N x M row-major, i.e. M x N column-major).
+        d_blas = torch.empty_like(ops.d)
+
+        def vendor():
+            with torch.cuda.stream(stream):
+                torch.mm(ops.b, ops.a.t(), out=d_blas)
+            return 0
+        fns[cublas] = vendor
     stream.synchronize()
     res = interleaved(stream, fns, pkg.flops(ops.m, ops.n, ops.k))
     if res is None:
         return {"unavailable": "launch failed"}
+    if cublas in fns:
+        out["vendor_cublas"] = {"tflops": res[cublas]["tflops"], "ours_over_cublas": 1.0 / res[cublas]["ratio_to_ours"]}
+        del fns[cublas]
     out["rounds"] = res["_rounds"]
     out["launches_per_burst"] = res["_launches_per_burst"]
     out["tflops_ours_interleaved"] = res["ours"]["tflops"]
