@@ -670,10 +670,21 @@ def run_tma_probe(pkg, dev, stream):
                         for _ in range(2)), key=lambda r: r["GBps"])
             pts.append({"box": [128, rows], "stages": stages, "bytes_in_flight_per_sm": best["bytes_in_flight_per_sm"],
                         "GBps": best["GBps"], "cycles_per_tma": best["cycles_per_tma"]})
-    del buf, flush
+    # L2-resident read rate of the probe (one warp per SM): a 96 MiB tensor (under the
+    # 126 MB L2) read three times without a flush, the last pass timed by the CTAs' own
+    # counters.  One warp does not saturate L2 (NVFP4 config 4 moves more under ncu at 57 %
+    # of L2 throughput), so this is a lower bound on the L2 roof, not the roof.
+    l2buf = torch.randint(0, 255, (96 << 20,), dtype=torch.uint8, device=dev)
+    l2pts = []
+    with torch.cuda.stream(stream):
+        for rows, stages in ((128, 3), (64, 6)):
+            r = [pkg.tma_read_probe(l2buf, box_rows=rows, stages=stages, device=dev) for _ in range(3)][-1]
+            l2pts.append({"box": [128, rows], "stages": stages, "bytes_per_clk_per_sm": r["bytes_per_clk_per_cta"],
+                          "sm_mhz": r["sm_mhz"], "GBps": r["GBps_in_kernel"]})
+    del buf, flush, l2buf
     torch.cuda.empty_cache()
     top = max(pts, key=lambda r: r["GBps"])
-    return {"points": pts, "roof_GBps": top["GBps"],
+    return {"points": pts, "roof_GBps": top["GBps"], "l2_resident_one_warp": l2pts,
             "reference_roof_GBps": 7260.0, "reference_source": "tma2d_throughput/tma2d_tput_results.csv:25 (ncu DRAM counter)",
             "method": "bytes / CUDA-event time of one probe launch over 2 GiB after an L2 flush"}
 

@@ -274,6 +274,11 @@ def tma_read_probe(buf, box_rows: int, stages: int, ctas_per_sm: int = 1, box_wi
             "bytes_in_flight_per_sm": ctas_per_sm * stages * tile_bytes, "bytes": tiles * tile_bytes,
             "ms": ms, "GBps": tiles * tile_bytes / (ms * 1e-3) / 1e9, "sm_cycles_avg": cyc,
             "tma_ops_avg": statistics.mean(x[2] for x in busy), "cycles_per_tma": statistics.mean(x[0] / x[2] for x in busy),
+            # from the CTAs' own counters (no launch overhead): bytes per SM clock, and the
+            # aggregate rate over the median CTA duration
+            "bytes_per_clk_per_cta": statistics.median(x[2] * tile_bytes / x[0] for x in busy),
+            "sm_mhz": statistics.median(x[0] / x[1] * 1e3 for x in busy if x[1] > 0),
+            "GBps_in_kernel": tiles * tile_bytes / statistics.median(x[1] for x in busy),
             "checksums": [x[3] for x in r], "tiles_per_cta": [x[2] for x in r]}
 
 
