@@ -826,8 +826,30 @@ gemm_sm100a_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const int ov_ch = ov / CW;
       const int first = (ov && cur_pos == 0) ? NCH - ov_ch : 0;
       const int release_after = ov ? ov_ch - 1 : NCH - 1;
+      int i0 = 0;
+      if (ov_ch == 2) {
+        // Both shared chunks into registers with one wait, then release the
+        // accumulator before either is converted and stored: the next tile's
+        // MMAs wait only for these two TMEM reads.
+        const int ca = (first % NCH) * CW, cb = ((first + 1) % NCH) * CW;
+        uint32_t ra[CW], rb[CW], o[CW / 2];
+        if constexpr (CW == 32) {
+          tmem_ld32(t_row + (uint32_t)(c_begin + ca), ra);
+          tmem_ld32(t_row + (uint32_t)(c_begin + cb), rb);
+        } else {
+          tmem_ld16(t_row + (uint32_t)(c_begin + ca), ra);
+          tmem_ld16(t_row + (uint32_t)(c_begin + cb), rb);
+        }
+        tmem_ld_wait();
+        release_acc();
+        if (beta != 0.f) convert_c(c_begin + ca, ra, o); else convert(ra, o);
+        emit(c_begin + ca, o);
+        if (beta != 0.f) convert_c(c_begin + cb, rb, o); else convert(rb, o);
+        emit(c_begin + cb, o);
+        i0 = 2;
+      }
 #pragma unroll 1
-      for (int i = 0; i < NCH; ++i) {
+      for (int i = i0; i < NCH; ++i) {
         const int ci = first + i < NCH ? first + i : first + i - NCH;
         const int cc = ci * CW;
         uint32_t r[CW], o[CW / 2];
